@@ -1,0 +1,151 @@
+/* liblumen_b200.so -- C-ABI of the B200 (sm_100a) inference-kernel path:
+ * BF16 GEMM, flash-attention forward and fused MoE forward.
+ *
+ * Conventions shared by every entry point
+ *   - plain pointers and sizes only; every pointer is a DEVICE pointer on the
+ *     current CUDA device unless a comment says "host";
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued on it and the
+ *     call returns without synchronising, so it can be captured in a CUDA graph;
+ *   - no entry point allocates or frees device memory; scratch is caller-owned
+ *     and sized with the matching *_bytes() helper;
+ *   - inputs are borrowed and never written;
+ *   - return value: LUMEN_B200_OK or a negative LUMEN_B200_E* code.  Errors found
+ *     by a running kernel (a bounded wait that gave up) are reported later by
+ *     lumen_b200_device_status().
+ *
+ * Each declaration names the interface of the reference (haohui/lumen-sosp26-ae,
+ * path relative to the reference tree) that it stands in for.
+ */
+#ifndef LUMEN_B200_H_
+#define LUMEN_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LUMEN_B200_OK 0
+#define LUMEN_B200_EINVAL (-1)       /* null pointer, non-positive size, misaligned pitch */
+#define LUMEN_B200_EWORKSPACE (-2)   /* scratch buffer smaller than *_bytes() asks for */
+#define LUMEN_B200_ECUDA (-3)        /* the CUDA runtime or driver refused a call */
+#define LUMEN_B200_EUNSUPPORTED (-4) /* shape outside what the kernels cover */
+#define LUMEN_B200_EDEVICE (-5)      /* a kernel recorded a wait that gave up */
+
+/* Library identification, e.g. "lumen_b200 0.1 sm_100a".  Host pointer, static storage. */
+const char* lumen_b200_version(void);
+
+/* Number of SMs of the current device, or a negative error code. */
+int lumen_b200_sm_count(void);
+
+/* Synchronises the current device, then stores the device status word in *status
+ * (host pointer): 0, or (wait site << 16 | CTA index) of the first kernel wait that
+ * gave up.  Returns LUMEN_B200_OK, LUMEN_B200_EDEVICE when *status != 0, or ECUDA.
+ * Stands in for the hipError_t that the reference's launch wrappers return
+ * (datasets/inference/gemm/ksearch/kernel.h:7-17) and that its bindings turn into
+ * a RuntimeError (datasets/inference/gemm/ksearch/best_binding.cpp:41-43). */
+int lumen_b200_device_status(int* status);
+
+/* Resets the device status word to 0 (synchronises). */
+int lumen_b200_clear_status(void);
+
+/* ------------------------------------------------------------------ GEMM -- */
+
+/* C[M,N] = A[M,K] * B[N,K]^T, bf16 inputs, fp32 accumulation, bf16 output rounded
+ * to nearest even.  Row-major with pitches lda, ldb, ldc in elements; lda and ldb
+ * must be multiples of 8 and A, B 16-byte aligned.  M <= 128 takes the
+ * weight-streaming split-K path, which uses `workspace`; with workspace == NULL
+ * that path runs unsplit.
+ * Replaces gemm_pipeline_transposed_b(A, B, out)
+ * (datasets/inference/gemm/lumen/amdgpu_gemm.py:872-923), the ksearch launch
+ * wrapper (datasets/inference/gemm/ksearch/kernel.h:7-17) and
+ * hipblaslt_bf16_mm_out(a, b, d)
+ * (datasets/inference/gemm/hipblaslt/hipblaslt_internal_ext.cpp:124-158). */
+int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                            int ldb, int ldc, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* Scratch bytes lumen_b200_gemm_bf16_nt wants for this shape on the current device
+ * (0 when the shape does not split).  Counterpart of the 32 MiB plan workspace at
+ * datasets/inference/gemm/hipblaslt/hipblaslt_internal_ext.cpp:12,110. */
+size_t lumen_b200_gemm_workspace_bytes(int M, int N, int K);
+
+/* ------------------------------------------------------------- attention -- */
+
+/* O = softmax(scale * Q K^T [+ causal mask]) V for Q,O [B,S,Hq,D] and K,V
+ * [B,S,Hkv,D], bf16, contiguous; query head h reads KV head h / (Hq / Hkv).
+ * D must be 128.  fp32 scores and softmax, bf16 output.
+ * Replaces flash_attn(q, k, v, seq_ptr, max_seq_len, out=)
+ * (datasets/inference/attention/lumen/attn_06_inst_scheduling.py:2144-2193) and
+ * run(q, k, v, sm_scale) (datasets/inference/attention/ksearch/best_binding.cpp:7-68). */
+int lumen_b200_fa_fwd_bf16(const void* Q, const void* K, const void* V, void* O, int B, int S,
+                           int Hq, int Hkv, int D, float scale, int causal, void* stream);
+
+/* ------------------------------------------------------------------- MoE -- */
+
+/* logits[T,E] (fp32) = x[T,H] * wr[E,H]^T, bf16 inputs.  E * H * 2 bytes must fit
+ * 200 KiB of shared memory.  The reference draws router scores directly
+ * (scripts/benchmark/backend_moe.py:125-130); this is the in-op router that
+ * precedes them for a model with a router matrix. */
+int lumen_b200_moe_router_logits(const void* x, const void* wr, void* logits, int T, int H, int E,
+                                 void* stream);
+
+/* topk_ids[T,k] (int32) and topk_weights[T,k] (fp32): the k largest logits of each
+ * row in descending order (ties: lower index first) and the softmax over those k.
+ * Replaces torch.topk(sorted=True) + softmax(topk_val)
+ * (scripts/benchmark/backend_moe.py:131-139). */
+int lumen_b200_moe_route_topk(const void* logits, void* topk_ids, void* topk_weights, int T, int E,
+                              int k, void* stream);
+
+size_t lumen_b200_moe_sort_scratch_bytes(int T, int E, int k);
+
+/* Stable expert-major sort of the T*k routes.  With P = T*k + E*32 - k and
+ * NB = ceil(P / 32):
+ *   sorted_token_ids[P]  int32  (slot << 24) | token, pads (k << 24) | T
+ *   sorted_weights[P]    fp32   route weight, pads 0
+ *   sorted_expert_ids[NB] int32 expert of each block of 32 sorted routes, unused -1
+ *   num_valid_ids[2]     int32  {padded route count, T}
+ * exactly as _build_sorted_routes (datasets/inference/moe/lumen/model.py:34-98)
+ * returns them, plus what the grouped GEMM and the combine read:
+ *   expert_offsets[E+1] int32  first sorted position of each expert (padded to 32)
+ *   expert_counts[E]    int32  routes of each expert
+ *   route_pos[T*k]      int32  sorted position of route t*k+slot */
+int lumen_b200_moe_sort_routes(const void* topk_ids, const void* topk_weights,
+                               void* sorted_token_ids, void* sorted_weights,
+                               void* sorted_expert_ids, void* num_valid_ids, void* expert_offsets,
+                               void* expert_counts, void* route_pos, void* scratch,
+                               size_t scratch_bytes, int T, int E, int k, void* stream);
+
+/* xs[pos,:] = x[token(sorted_token_ids[pos]),:] for pos < num_valid_ids[0]; pad rows
+ * become 0.  max_rows = T*k + E*32 - k bounds the launch.  Replaces the gather in
+ * _input_fetch_async (datasets/inference/moe/lumen/fused_moe.py:246-271). */
+int lumen_b200_moe_permute_rows(const void* x, const void* sorted_token_ids,
+                                const void* num_valid_ids, void* xs, int T, int H, int max_rows,
+                                void* stream);
+
+/* Per-expert GEMM over rows in expert order:
+ *   gated == 0:  out[r, 0:N] = acts[r, 0:K] * W_e[0:N, 0:K]^T
+ *   gated != 0:  out[r, 0:N] = silu(acts[r] * W_e[0:N]^T) * (acts[r] * W_e[N:2N]^T)
+ * for every row r of expert e (expert_offsets[e] <= r < expert_offsets[e] +
+ * expert_counts[e]); `weights` is [E, w_rows, K] bf16 with w_rows = N (plain) or 2N
+ * (gate rows first, up rows second, the w1_q layout of
+ * scripts/benchmark/backend_moe.py:162-171).  acts is [max_rows, K], out
+ * [max_rows, N].  rows_hint = expected rows per expert, picks the tile orientation.
+ * Replaces stage 1 + SiLU (gated) and stage 2 (plain) of
+ * _fused_moe_blockscale_fp8_kernel (datasets/inference/moe/lumen/fused_moe.py:1100-1335). */
+int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights, void* out,
+                                const void* expert_offsets, const void* expert_counts,
+                                int max_rows, int E, int N, int K, int gated, int rows_hint,
+                                void* stream);
+
+/* out[t,:] = sum_slot topk_weights[t,slot] * y[route_pos[t*k+slot],:], fp32 sum in
+ * slot order, bf16 out.  Replaces the atomic write-back of _stage2_write_back
+ * (datasets/inference/moe/lumen/fused_moe.py:864-888) with a deterministic gather. */
+int lumen_b200_moe_combine(const void* y, const void* route_pos, const void* topk_weights,
+                           void* out, int T, int H, int k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUMEN_B200_H_ */

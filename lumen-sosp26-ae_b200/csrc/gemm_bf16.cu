@@ -1,0 +1,192 @@
+// Host launchers and C-ABI entry points of the BF16 contraction core: the dense
+// GEMM C = A * B^T and the per-expert (grouped) GEMMs of the MoE.
+#include "gemm_bf16.cuh"
+#include "lumen_b200_internal.h"
+
+namespace b200 {
+namespace {
+
+template <int BN, int STAGES, bool SWAP, bool GATED, bool GROUPED>
+int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& args, int grid,
+                cudaStream_t st) {
+  auto kern = gemm_bf16_kernel<BN, STAGES, SWAP, GATED, GROUPED>;
+  constexpr size_t smem = gemm_smem_bytes<BN, STAGES, SWAP, GATED, GROUPED>();
+  static_assert(smem <= 227 * 1024, "stage ring does not fit shared memory");
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LUMEN_B200_ECUDA;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+    configured[dev] = true;
+  }
+  kern<<<grid, kGemmThreads, smem, st>>>(mp, mq, args);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+inline int ceil_div_h(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+// swapped dense path: tile geometry and split-K plan for M <= 128
+struct SwapPlan {
+  int bn;       // activation rows per tile (UMMA N)
+  int tiles;    // output tiles
+  int splits;   // K slices per tile
+  size_t counter_bytes;
+  size_t partial_bytes;
+};
+
+SwapPlan plan_swap(int M, int N, int K, int sms) {
+  SwapPlan p;
+  p.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  p.tiles = ceil_div_h(N, kBlockP) * ceil_div_h(M, p.bn);
+  const int k_blocks = ceil_div_h(K, kBlockK);
+  int splits = sms / p.tiles;
+  const int max_splits = k_blocks / 4 > 0 ? k_blocks / 4 : 1;  // at least 4 K blocks per slice
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  p.splits = splits;
+  p.counter_bytes = (size_t(p.tiles) * sizeof(int) + 255) / 256 * 256;
+  p.partial_bytes = splits > 1 ? size_t(p.tiles) * splits * p.bn * kBlockP * sizeof(float) : 0;
+  return p;
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" size_t lumen_b200_gemm_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > 128) return 0;
+  const int sms = device_sm_count();
+  if (sms <= 0) return 0;
+  const SwapPlan p = plan_swap(M, N, K, sms);
+  return p.splits > 1 ? p.counter_bytes + p.partial_bytes : 0;
+}
+
+extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, int M, int N, int K,
+                                        int lda, int ldb, int ldc, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LUMEN_B200_EINVAL;
+  if (lda < K || ldb < K || ldc < N) return LUMEN_B200_EINVAL;
+  if (lda % 8 != 0 || ldb % 8 != 0) return LUMEN_B200_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return LUMEN_B200_EINVAL;
+  const int sms = device_sm_count();
+  int* status = device_status_word();
+  if (sms <= 0 || !status) return LUMEN_B200_ECUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  GemmArgs args{};
+  args.out = static_cast<__nv_bfloat16*>(C);
+  args.ldo = ldc;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.splits = 1;
+  args.status = status;
+
+  CUtensorMap mp, mq;
+  if (M > 128) {
+    // P = A (128-row boxes), Q = B (256-row boxes)
+    if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
+    if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, 256) != 0) return LUMEN_B200_ECUDA;
+    const int units = ceil_div_h(M, kBlockP) * ceil_div_h(N, 256);
+    const int grid = units < sms ? units : sms;
+    return launch_gemm<256, 4, false, false, false>(mp, mq, args, grid, st);
+  }
+
+  // weight-streaming path: P = B (weights on the TMEM lanes), Q = A
+  SwapPlan plan = plan_swap(M, N, K, sms);
+  if (plan.splits > 1) {
+    if (!workspace || workspace_bytes < plan.counter_bytes + plan.partial_bytes) {
+      if (workspace) return LUMEN_B200_EWORKSPACE;
+      plan.splits = 1;
+    }
+  }
+  if (plan.splits > 1) {
+    args.splits = plan.splits;
+    args.counters = static_cast<int*>(workspace);
+    args.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + plan.counter_bytes);
+    if (cudaMemsetAsync(args.counters, 0, plan.counter_bytes, st) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+  }
+  if (encode_tmap_bf16_2d(&mp, B, N, K, ldb, kBlockP) != 0) return LUMEN_B200_ECUDA;
+  if (encode_tmap_bf16_2d(&mq, A, M, K, lda, plan.bn) != 0) return LUMEN_B200_ECUDA;
+  const int units = plan.tiles * plan.splits;
+  const int grid = units < sms ? units : sms;
+  switch (plan.bn) {
+    case 16:
+      return launch_gemm<16, 10, true, false, false>(mp, mq, args, grid, st);
+    case 32:
+      return launch_gemm<32, 10, true, false, false>(mp, mq, args, grid, st);
+    case 64:
+      return launch_gemm<64, 8, true, false, false>(mp, mq, args, grid, st);
+    default:
+      return launch_gemm<128, 6, true, false, false>(mp, mq, args, grid, st);
+  }
+}
+
+extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights, void* out,
+                                            const void* expert_offsets, const void* expert_counts,
+                                            int max_rows, int E, int N, int K, int gated,
+                                            int rows_hint, void* stream) {
+  if (!acts || !weights || !out || !expert_offsets || !expert_counts) return LUMEN_B200_EINVAL;
+  if (max_rows <= 0 || E <= 0 || E > kMaxExperts || N <= 0 || K <= 0 || K % 8 != 0)
+    return LUMEN_B200_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(acts) & 15) || (reinterpret_cast<uintptr_t>(weights) & 15))
+    return LUMEN_B200_EINVAL;
+  const int sms = device_sm_count();
+  int* status = device_status_word();
+  if (sms <= 0 || !status) return LUMEN_B200_ECUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const int w_rows = gated ? 2 * N : N;
+  GemmArgs args{};
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.ldo = N;
+  args.M = 0;
+  args.N = N;
+  args.K = K;
+  args.splits = 1;
+  args.expert_offsets = static_cast<const int*>(expert_offsets);
+  args.expert_counts = static_cast<const int*>(expert_counts);
+  args.num_experts = E;
+  args.w_rows_per_expert = w_rows;
+  args.up_row_offset = N;
+  args.status = status;
+
+  const uint64_t w_total_rows = uint64_t(E) * w_rows;
+  CUtensorMap mp, mq;
+  const int grid = sms;
+  if (rows_hint > 64) {
+    // tokens on the TMEM lanes, 128 rows per unit
+    if (encode_tmap_bf16_2d(&mp, acts, max_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
+    if (encode_tmap_bf16_2d(&mq, weights, w_total_rows, K, K, gated ? 128 : 256) != 0)
+      return LUMEN_B200_ECUDA;
+    return gated ? launch_gemm<256, 4, false, true, true>(mp, mq, args, grid, st)
+                 : launch_gemm<256, 4, false, false, true>(mp, mq, args, grid, st);
+  }
+  // few rows per expert: weights on the TMEM lanes
+  const int bn = rows_hint <= 16 ? 16 : rows_hint <= 32 ? 32 : 64;
+  if (encode_tmap_bf16_2d(&mp, weights, w_total_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
+  if (encode_tmap_bf16_2d(&mq, acts, max_rows, K, K, bn) != 0) return LUMEN_B200_ECUDA;
+  if (gated) {
+    switch (bn) {
+      case 16:
+        return launch_gemm<16, 6, true, true, true>(mp, mq, args, grid, st);
+      case 32:
+        return launch_gemm<32, 6, true, true, true>(mp, mq, args, grid, st);
+      default:
+        return launch_gemm<64, 5, true, true, true>(mp, mq, args, grid, st);
+    }
+  }
+  switch (bn) {
+    case 16:
+      return launch_gemm<16, 10, true, false, true>(mp, mq, args, grid, st);
+    case 32:
+      return launch_gemm<32, 10, true, false, true>(mp, mq, args, grid, st);
+    default:
+      return launch_gemm<64, 8, true, false, true>(mp, mq, args, grid, st);
+  }
+}

@@ -1,0 +1,468 @@
+// Memory-bound kernels of the fused MoE forward: router logits, top-k softmax
+// routing, the stable expert-major sort of the T*k routes (the permutation that
+// _build_sorted_routes in datasets/inference/moe/lumen/model.py:34-98 of the
+// reference defines), the row gather into expert order and the weighted combine.
+//
+// All of them are HBM-bound integer / byte movers: vectorised 16-byte accesses,
+// one warp or one CTA per row, no tensor cores.
+#include "lumen_b200_internal.h"
+
+namespace b200 {
+
+constexpr int kRouteChunk = 1024;  // routes ranked by one CTA
+constexpr int kRouteGroup = 32;    // the reference pads every expert to a multiple of 32 routes
+
+// ---------------------------------------------------------------------------
+// router logits: logits[t][e] = sum_h x[t][h] * wr[e][h]   (bf16 in, fp32 out)
+// One warp per pair of tokens; the router matrix is staged once per CTA in
+// shared memory.  Mirrors `logits = x.float() @ Wr.float().T`.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    moe_router_logits_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wr,
+                             float* __restrict__ logits, int T, int H, int E) {
+  extern __shared__ uint4 s_wr[];  // [E][H/8] 16-byte chunks
+  const int chunks = H / 8;
+  for (int i = threadIdx.x; i < E * chunks; i += blockDim.x)
+    s_wr[i] = reinterpret_cast<const uint4*>(wr)[i];
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int warps_per_cta = blockDim.x >> 5;
+  const int gwarp = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+  const int nwarps = gridDim.x * warps_per_cta;
+
+  for (int t0 = gwarp * 2; t0 < T; t0 += nwarps * 2) {
+    const bool has1 = (t0 + 1) < T;
+    const uint4* x0 = reinterpret_cast<const uint4*>(x + size_t(t0) * H);
+    const uint4* x1 = reinterpret_cast<const uint4*>(x + size_t(has1 ? t0 + 1 : t0) * H);
+    for (int e0 = 0; e0 < E; e0 += 8) {
+      float acc0[8], acc1[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
+      for (int c = lane; c < chunks; c += 32) {
+        const uint4 a = __ldg(x0 + c);
+        const uint4 b = __ldg(x1 + c);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+        float af[8], bf[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 fa = __bfloat1622float2(a2[j]);
+          const float2 fb = __bfloat1622float2(b2[j]);
+          af[2 * j] = fa.x;
+          af[2 * j + 1] = fa.y;
+          bf[2 * j] = fb.x;
+          bf[2 * j + 1] = fb.y;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e0 + e < E) {
+            const uint4 w = s_wr[(e0 + e) * chunks + c];
+            const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 fw = __bfloat1622float2(w2[j]);
+              acc0[e] = fmaf(af[2 * j], fw.x, acc0[e]);
+              acc0[e] = fmaf(af[2 * j + 1], fw.y, acc0[e]);
+              acc1[e] = fmaf(bf[2 * j], fw.x, acc1[e]);
+              acc1[e] = fmaf(bf[2 * j + 1], fw.y, acc1[e]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+          acc0[e] += __shfl_xor_sync(0xffffffffu, acc0[e], d);
+          acc1[e] += __shfl_xor_sync(0xffffffffu, acc1[e], d);
+        }
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e0 + e < E) {
+            logits[size_t(t0) * E + e0 + e] = acc0[e];
+            if (has1) logits[size_t(t0 + 1) * E + e0 + e] = acc1[e];
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// top-k + softmax over the selected logits.  One warp per token.
+//   ids[t][j]     = index of the j-th largest logit (ties: lowest index first)
+//   weights[t][j] = softmax over the k selected logits
+// Mirrors torch.topk(sorted=True) followed by softmax(topk_val)
+// (scripts/benchmark/backend_moe.py:131-139 of the reference).
+// VPL = logits held per lane; supports E <= 32 * VPL.
+// ---------------------------------------------------------------------------
+template <int VPL>
+__global__ void __launch_bounds__(256)
+    moe_topk_softmax_kernel(const float* __restrict__ logits, int* __restrict__ ids,
+                            float* __restrict__ weights, int T, int E, int k) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const float* row = logits + size_t(t) * E;
+  float v[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = (e < E) ? row[e] : -INFINITY;
+  }
+  uint32_t taken = 0;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+    if (i * 32 + lane >= E) taken |= (1u << i);
+
+  float my_val = 0.f;
+  int my_idx = 0;
+  float top_val = 0.f;
+  for (int j = 0; j < k; ++j) {
+    // lane-local best among values not yet taken
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const bool free_slot = !((taken >> i) & 1u);
+      const int e = i * 32 + lane;
+      if (free_slot && (bi == 0x7fffffff || v[i] > bv)) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+    // warp argmax, ties to the lower index
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+      const bool take = (oi != 0x7fffffff) && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi));
+      if (take) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (j == 0) top_val = bv;
+    if (lane == j) {
+      my_val = bv;
+      my_idx = bi;
+    }
+  }
+  const float ex = (lane < k) ? expf(my_val - top_val) : 0.f;
+  float sum = ex;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+  if (lane < k) {
+    ids[size_t(t) * k + lane] = my_idx;
+    weights[size_t(t) * k + lane] = ex / sum;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// stable expert-major sort of the routes, in three small kernels
+// ---------------------------------------------------------------------------
+// (1) per-chunk histogram: block_hist[b][e] = routes of chunk b that go to expert e
+__global__ void __launch_bounds__(kRouteChunk)
+    moe_block_hist_kernel(const int* __restrict__ ids, int* __restrict__ block_hist, int routes,
+                          int E) {
+  extern __shared__ int s_hist[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
+  __syncthreads();
+  const int r = blockIdx.x * kRouteChunk + threadIdx.x;
+  if (r < routes) {
+    const int e = ids[r];
+    if (e >= 0 && e < E) atomicAdd(&s_hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) block_hist[size_t(blockIdx.x) * E + e] = s_hist[e];
+}
+
+// (2) one CTA: per-expert scan over chunks, padded exclusive scan over experts,
+//     block -> expert map, and the pad fill of the sorted arrays.
+__global__ void __launch_bounds__(1024)
+    moe_scan_kernel(int* __restrict__ block_hist /* in: counts, out: chunk bases */,
+                    int* __restrict__ expert_offsets, int* __restrict__ expert_counts,
+                    int* __restrict__ sorted_token_ids, float* __restrict__ sorted_weights,
+                    int* __restrict__ sorted_expert_ids, int* __restrict__ num_valid_ids, int T, int k,
+                    int E, int nchunks) {
+  __shared__ int s_warp[32];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+
+  const int max_padded = T * k + E * kRouteGroup - k;
+  const int max_blocks = (max_padded + kRouteGroup - 1) / kRouteGroup;
+  const int sentinel = (k << 24) | T;
+  for (int i = tid; i < max_padded; i += blockDim.x) {
+    sorted_token_ids[i] = sentinel;
+    sorted_weights[i] = 0.f;
+  }
+  for (int i = tid; i < max_blocks; i += blockDim.x) sorted_expert_ids[i] = -1;
+
+  int carry_all = 0;  // padded routes of the experts handled in earlier rounds
+  for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+    const int e = e0 + tid;
+    int cnt = 0;
+    if (e < E) {
+      for (int b = 0; b < nchunks; ++b) {
+        const int v = block_hist[size_t(b) * E + e];
+        block_hist[size_t(b) * E + e] = cnt;
+        cnt += v;
+      }
+    }
+    const int padded = (cnt + kRouteGroup - 1) / kRouteGroup * kRouteGroup;
+    // block-wide exclusive scan of `padded`
+    int incl = padded;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_warp[lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= d) w += o;
+      }
+      s_warp[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int warp_base = (warp == 0) ? 0 : s_warp[warp - 1];
+    const int off = carry_all + warp_base + incl - padded;
+    const int round_total = s_warp[31];
+    if (e < E) {
+      expert_offsets[e] = off;
+      expert_counts[e] = cnt;
+    }
+    __syncthreads();  // the pad fill above is complete before any block id is written
+    if (e < E) {
+      for (int b = off / kRouteGroup; b < (off + padded) / kRouteGroup; ++b) sorted_expert_ids[b] = e;
+    }
+    carry_all += round_total;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    expert_offsets[E] = carry_all;
+    num_valid_ids[0] = carry_all;
+    num_valid_ids[1] = T;
+  }
+}
+
+// (3) stable rank inside the chunk + scatter.  Route r = t*k + slot keeps the
+//     (token ascending, slot ascending) order inside its expert.
+__global__ void __launch_bounds__(kRouteChunk)
+    moe_rank_scatter_kernel(const int* __restrict__ ids, const float* __restrict__ weights,
+                            const int* __restrict__ chunk_base, const int* __restrict__ expert_offsets,
+                            int* __restrict__ sorted_token_ids, float* __restrict__ sorted_weights,
+                            int* __restrict__ route_pos, int routes, int k, int E) {
+  __shared__ int s_e[kRouteChunk];
+  const int i = threadIdx.x;
+  const int r = blockIdx.x * kRouteChunk + i;
+  int e = -1;
+  if (r < routes) {
+    e = ids[r];
+    if (e < 0 || e >= E) e = -1;
+  }
+  s_e[i] = e;
+  __syncthreads();
+  // rank = number of earlier routes of this chunk with the same expert
+  const int warp_last = (i | 31);
+  int rank = 0;
+  for (int j = 0; j < warp_last; ++j) rank += (j < i && s_e[j] == e) ? 1 : 0;
+  if (e >= 0) {
+    const int pos = expert_offsets[e] + chunk_base[size_t(blockIdx.x) * E + e] + rank;
+    const int token = r / k;
+    const int slot = r - token * k;
+    sorted_token_ids[pos] = (slot << 24) | token;
+    sorted_weights[pos] = weights[r];
+    route_pos[r] = pos;
+  } else if (r < routes) {
+    route_pos[r] = -1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// gather rows into expert order: xs[pos][:] = x[token(pos)][:], pad rows = 0.
+// One CTA per sorted position; 16-byte accesses.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    moe_permute_rows_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted_token_ids,
+                            const int* __restrict__ num_valid_ids, __nv_bfloat16* __restrict__ xs, int T,
+                            int H) {
+  const int total = num_valid_ids[0];
+  const int chunks = H / 8;
+  for (int pos = blockIdx.x; pos < total; pos += gridDim.x) {
+    const int token = sorted_token_ids[pos] & 0xffffff;
+    uint4* dst = reinterpret_cast<uint4*>(xs + size_t(pos) * H);
+    if (token < T) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + size_t(token) * H);
+      for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+    } else {
+      for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// weighted combine: out[t][:] = sum_slot w[t][slot] * y[route_pos[t*k+slot]][:]
+// fp32 accumulation in slot order (deterministic), bf16 round-to-nearest-even out.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ route_pos,
+                       const float* __restrict__ weights, __nv_bfloat16* __restrict__ out, int T, int H,
+                       int k) {
+  const int chunks = H / 8;
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int s = 0; s < k; ++s) {
+        const int pos = route_pos[size_t(t) * k + s];
+        if (pos < 0) continue;
+        const float w = weights[size_t(t) * k + s];
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + size_t(pos) * H) + c);
+        const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(q2[j]);
+          acc[2 * j] = fmaf(w, f.x, acc[2 * j]);
+          acc[2 * j + 1] = fmaf(w, f.y, acc[2 * j + 1]);
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(out + size_t(t) * H)[c] = o;
+    }
+  }
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+// ===========================================================================
+// C-ABI
+// ===========================================================================
+extern "C" int lumen_b200_moe_router_logits(const void* x, const void* wr, void* logits, int T, int H,
+                                             int E, void* stream) {
+  if (!x || !wr || !logits || T <= 0 || H <= 0 || E <= 0 || H % 8 != 0) return LUMEN_B200_EINVAL;
+  const size_t smem = size_t(E) * H * 2;
+  if (smem > 200 * 1024) return LUMEN_B200_EUNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(moe_router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+    attr_set[dev] = true;
+  }
+  const int sms = device_sm_count();
+  const int warps = 8;
+  int grid = (T + warps * 2 - 1) / (warps * 2);
+  if (grid > sms) grid = sms;
+  moe_router_logits_kernel<<<grid, warps * 32, smem, st>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(wr),
+      static_cast<float*>(logits), T, H, E);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_route_topk(const void* logits, void* topk_ids, void* topk_weights, int T,
+                                          int E, int k, void* stream) {
+  if (!logits || !topk_ids || !topk_weights || T <= 0 || E <= 0 || k <= 0 || k > E || k > 32 ||
+      E > 1024)
+    return LUMEN_B200_EINVAL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int warps = 8;
+  const int grid = (T + warps - 1) / warps;
+  const float* lg = static_cast<const float*>(logits);
+  int* ids = static_cast<int*>(topk_ids);
+  float* w = static_cast<float*>(topk_weights);
+  if (E <= 32)
+    moe_topk_softmax_kernel<1><<<grid, warps * 32, 0, st>>>(lg, ids, w, T, E, k);
+  else if (E <= 256)
+    moe_topk_softmax_kernel<8><<<grid, warps * 32, 0, st>>>(lg, ids, w, T, E, k);
+  else
+    moe_topk_softmax_kernel<32><<<grid, warps * 32, 0, st>>>(lg, ids, w, T, E, k);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" size_t lumen_b200_moe_sort_scratch_bytes(int T, int E, int k) {
+  if (T <= 0 || E <= 0 || k <= 0) return 0;
+  const size_t routes = size_t(T) * k;
+  const size_t nchunks = (routes + kRouteChunk - 1) / kRouteChunk;
+  return nchunks * E * sizeof(int);
+}
+
+extern "C" int lumen_b200_moe_sort_routes(const void* topk_ids, const void* topk_weights,
+                                           void* sorted_token_ids, void* sorted_weights,
+                                           void* sorted_expert_ids, void* num_valid_ids,
+                                           void* expert_offsets, void* expert_counts, void* route_pos,
+                                           void* scratch, size_t scratch_bytes, int T, int E, int k,
+                                           void* stream) {
+  if (!topk_ids || !topk_weights || !sorted_token_ids || !sorted_weights || !sorted_expert_ids ||
+      !num_valid_ids || !expert_offsets || !expert_counts || !route_pos || !scratch)
+    return LUMEN_B200_EINVAL;
+  // token index must fit the 24-bit field of the packed route id
+  if (T <= 0 || E <= 0 || k <= 0 || E > kMaxExperts || T >= (1 << 24) || k > 127)
+    return LUMEN_B200_EINVAL;
+  if (scratch_bytes < lumen_b200_moe_sort_scratch_bytes(T, E, k)) return LUMEN_B200_EWORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int routes = T * k;
+  const int nchunks = (routes + kRouteChunk - 1) / kRouteChunk;
+  int* hist = static_cast<int*>(scratch);
+  moe_block_hist_kernel<<<nchunks, kRouteChunk, E * sizeof(int), st>>>(
+      static_cast<const int*>(topk_ids), hist, routes, E);
+  moe_scan_kernel<<<1, 1024, 0, st>>>(hist, static_cast<int*>(expert_offsets),
+                                      static_cast<int*>(expert_counts),
+                                      static_cast<int*>(sorted_token_ids),
+                                      static_cast<float*>(sorted_weights),
+                                      static_cast<int*>(sorted_expert_ids),
+                                      static_cast<int*>(num_valid_ids), T, k, E, nchunks);
+  moe_rank_scatter_kernel<<<nchunks, kRouteChunk, 0, st>>>(
+      static_cast<const int*>(topk_ids), static_cast<const float*>(topk_weights), hist,
+      static_cast<const int*>(expert_offsets), static_cast<int*>(sorted_token_ids),
+      static_cast<float*>(sorted_weights), static_cast<int*>(route_pos), routes, k, E);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_permute_rows(const void* x, const void* sorted_token_ids,
+                                            const void* num_valid_ids, void* xs, int T, int H,
+                                            int max_rows, void* stream) {
+  if (!x || !sorted_token_ids || !num_valid_ids || !xs || T <= 0 || H <= 0 || H % 8 != 0 ||
+      max_rows <= 0)
+    return LUMEN_B200_EINVAL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = device_sm_count();
+  int grid = max_rows < sms * 16 ? max_rows : sms * 16;
+  moe_permute_rows_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                static_cast<const int*>(sorted_token_ids),
+                                                static_cast<const int*>(num_valid_ids),
+                                                static_cast<__nv_bfloat16*>(xs), T, H);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_combine(const void* y, const void* route_pos, const void* topk_weights,
+                                       void* out, int T, int H, int k, void* stream) {
+  if (!y || !route_pos || !topk_weights || !out || T <= 0 || H <= 0 || H % 8 != 0 || k <= 0)
+    return LUMEN_B200_EINVAL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = device_sm_count();
+  int grid = T < sms * 16 ? T : sms * 16;
+  moe_combine_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(y),
+                                           static_cast<const int*>(route_pos),
+                                           static_cast<const float*>(topk_weights),
+                                           static_cast<__nv_bfloat16*>(out), T, H, k);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}

@@ -1,0 +1,102 @@
+"""Host side of the BF16 GEMM  C[M,N] = A[M,K] * B[N,K]^T  (fp32 accumulation).
+
+`gemm_pipeline_transposed_b` keeps the name, argument meaning and error behaviour of
+the reference's host wrapper (datasets/inference/gemm/lumen/amdgpu_gemm.py:872-923):
+bf16 2-D inputs, B stored [N,K], optional caller-owned `out`, ValueError on a bad
+dtype / rank / shape.  The work is done by lumen_b200_gemm_bf16_nt in
+liblumen_b200.so on the current CUDA stream; nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _cabi
+
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Per-device, per-stream split-K scratch, grown on demand (never shrunk)."""
+    if nbytes == 0:
+        return None
+    key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def gemm_workspace_bytes(m: int, n: int, k: int) -> int:
+    return int(_cabi.load().lumen_b200_gemm_workspace_bytes(m, n, k))
+
+
+def gemm_pipeline_transposed_b(
+    A: torch.Tensor,
+    B: torch.Tensor,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    if A.dtype != torch.bfloat16:
+        raise ValueError(f"A must have dtype torch.bfloat16, got {A.dtype}.")
+    if B.dtype != torch.bfloat16:
+        raise ValueError(f"B must have dtype torch.bfloat16, got {B.dtype}.")
+    if A.ndim != 2:
+        raise ValueError(f"A must be 2D, got shape {tuple(A.shape)}.")
+    if B.ndim != 2:
+        raise ValueError(f"B must be 2D, got shape {tuple(B.shape)}.")
+    m, k = A.shape
+    n = B.shape[0]
+    if B.shape[1] != k:
+        raise ValueError(f"B.shape[1] must equal K={k}, got {B.shape[1]}.")
+    if not A.is_cuda or not B.is_cuda:
+        raise ValueError("A and B must be CUDA tensors: this operator has no CPU path.")
+    if B.device != A.device:
+        raise ValueError(f"B must be on device {A.device}, got {B.device}.")
+    if m == 0 or n == 0 or k == 0:
+        raise ValueError(f"empty GEMM is not supported: M={m}, N={n}, K={k}.")
+    if A.stride(1) != 1 or B.stride(1) != 1:
+        raise ValueError("A and B must be row-major (unit stride along K).")
+    if k % 8 != 0 and (A.stride(0) % 8 != 0 or B.stride(0) % 8 != 0):
+        raise ValueError(f"row pitch must be a multiple of 8 elements (16 bytes); K={k}.")
+    if A.stride(0) % 8 != 0 or B.stride(0) % 8 != 0:
+        raise ValueError("row pitch of A and B must be a multiple of 8 elements (16 bytes).")
+
+    out_shape = (m, n)
+    if out is None:
+        out = torch.empty(out_shape, dtype=torch.bfloat16, device=A.device)
+    elif tuple(out.shape) != out_shape:
+        raise ValueError(f"out must have shape {out_shape}, got {tuple(out.shape)}.")
+    elif out.dtype != torch.bfloat16:
+        raise ValueError(f"out must have dtype torch.bfloat16, got {out.dtype}.")
+    elif out.device != A.device:
+        raise ValueError(f"out must be on device {A.device}, got {out.device}.")
+    elif out.stride(1) != 1:
+        raise ValueError("out must be row-major.")
+
+    lib = _cabi.load()
+    with torch.cuda.device(A.device):
+        ws = _workspace(A.device, int(lib.lumen_b200_gemm_workspace_bytes(m, n, k)))
+        stream = torch.cuda.current_stream(A.device).cuda_stream
+        rc = lib.lumen_b200_gemm_bf16_nt(
+            A.data_ptr(), B.data_ptr(), out.data_ptr(), m, n, k,
+            A.stride(0), B.stride(0), out.stride(0),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            stream,
+        )
+    _cabi.check("lumen_b200_gemm_bf16_nt", rc)
+    return out
+
+
+def device_status() -> int:
+    """Synchronise and return the device status word (0 = no kernel wait gave up)."""
+    import ctypes
+
+    st = ctypes.c_int(0)
+    rc = _cabi.load().lumen_b200_device_status(ctypes.byref(st))
+    if rc not in (_cabi.OK, _cabi.EDEVICE):
+        _cabi.check("lumen_b200_device_status", rc)
+    return int(st.value)
+
+
+def clear_status() -> None:
+    _cabi.check("lumen_b200_clear_status", _cabi.load().lumen_b200_clear_status())

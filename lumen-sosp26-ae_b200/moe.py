@@ -1,0 +1,228 @@
+"""Host side of the fused MoE forward (bf16, in-op router).
+
+Pipeline, all on the current CUDA stream and with no host read of device data, so
+the whole forward can be captured in a CUDA graph:
+
+    router logits -> top-k softmax -> stable expert-major sort -> row gather
+    -> grouped GEMM (w1|w3, SiLU gate fused) -> grouped GEMM (w2) -> weighted combine
+
+The sorted-route arrays are the ones the reference builds on the host with
+_build_sorted_routes (datasets/inference/moe/lumen/model.py:34-98); here they are
+produced on the device and are what the grouped GEMMs actually consume.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _cabi
+
+ROUTE_GROUP_SIZE = 32
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("MoE operators need CUDA tensors: there is no CPU path.")
+        if t.device != dev:
+            raise ValueError(f"all tensors must be on {dev}, got {t.device}.")
+        if not t.is_contiguous():
+            raise ValueError("MoE operators need contiguous tensors.")
+    return dev
+
+
+def router_logits(x: torch.Tensor, w_router: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """logits[T,E] fp32 = x[T,H] @ w_router[E,H]^T (bf16 inputs)."""
+    dev = _need_cuda(x, w_router)
+    if x.dtype != torch.bfloat16 or w_router.dtype != torch.bfloat16:
+        raise ValueError("router_logits expects bf16 x and w_router.")
+    T, H = x.shape
+    E = w_router.shape[0]
+    if w_router.shape[1] != H:
+        raise ValueError(f"w_router must be [E,{H}], got {tuple(w_router.shape)}.")
+    if out is None:
+        out = torch.empty((T, E), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _cabi.load().lumen_b200_moe_router_logits(
+            x.data_ptr(), w_router.data_ptr(), out.data_ptr(), T, H, E, _stream(dev))
+    _cabi.check("lumen_b200_moe_router_logits", rc)
+    return out
+
+
+def route_topk(logits: torch.Tensor, topk: int,
+               ids_out: torch.Tensor | None = None,
+               weights_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(topk_ids int32 [T,k], topk_weights fp32 [T,k]) = topk(sorted) + softmax(topk values)."""
+    dev = _need_cuda(logits)
+    if logits.dtype != torch.float32 or logits.ndim != 2:
+        raise ValueError("route_topk expects fp32 logits [T,E].")
+    T, E = logits.shape
+    if topk > E:
+        raise ValueError(f"topk ({topk}) must be <= experts ({E})")
+    ids = ids_out if ids_out is not None else torch.empty((T, topk), dtype=torch.int32, device=dev)
+    w = weights_out if weights_out is not None else torch.empty((T, topk), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _cabi.load().lumen_b200_moe_route_topk(
+            logits.data_ptr(), ids.data_ptr(), w.data_ptr(), T, E, topk, _stream(dev))
+    _cabi.check("lumen_b200_moe_route_topk", rc)
+    return ids, w
+
+
+@dataclass
+class SortedRoutes:
+    """Device-side result of the route sort; first four fields are the reference's tuple."""
+
+    sorted_token_ids: torch.Tensor
+    sorted_weights: torch.Tensor
+    sorted_expert_ids: torch.Tensor
+    num_valid_ids: torch.Tensor
+    expert_offsets: torch.Tensor
+    expert_counts: torch.Tensor
+    route_pos: torch.Tensor
+
+    def as_reference_tuple(self):
+        return (self.sorted_token_ids, self.sorted_weights, self.sorted_expert_ids, self.num_valid_ids)
+
+
+def max_padded_routes(tokens: int, topk: int, experts: int) -> int:
+    return tokens * topk + experts * ROUTE_GROUP_SIZE - topk
+
+
+def alloc_sorted_routes(tokens: int, topk: int, experts: int, device: torch.device) -> SortedRoutes:
+    P = max_padded_routes(tokens, topk, experts)
+    nb = (P + ROUTE_GROUP_SIZE - 1) // ROUTE_GROUP_SIZE
+    i32 = dict(dtype=torch.int32, device=device)
+    return SortedRoutes(
+        sorted_token_ids=torch.empty((P,), **i32),
+        sorted_weights=torch.empty((P,), dtype=torch.float32, device=device),
+        sorted_expert_ids=torch.empty((nb,), **i32),
+        num_valid_ids=torch.empty((2,), **i32),
+        expert_offsets=torch.empty((experts + 1,), **i32),
+        expert_counts=torch.empty((experts,), **i32),
+        route_pos=torch.empty((tokens * topk,), **i32),
+    )
+
+
+def build_sorted_routes(*, topk_ids: torch.Tensor, topk_weights: torch.Tensor, experts: int,
+                        out: SortedRoutes | None = None,
+                        scratch: torch.Tensor | None = None) -> SortedRoutes:
+    """Device version of _build_sorted_routes (same keyword arguments)."""
+    dev = _need_cuda(topk_ids, topk_weights)
+    if topk_ids.dtype != torch.int32 or topk_weights.dtype != torch.float32:
+        raise ValueError("topk_ids must be int32 and topk_weights float32.")
+    tokens, topk = topk_ids.shape
+    if tuple(topk_weights.shape) != (tokens, topk):
+        raise ValueError("topk_weights shape mismatch.")
+    lib = _cabi.load()
+    need = int(lib.lumen_b200_moe_sort_scratch_bytes(tokens, experts, topk))
+    if scratch is None:
+        scratch = torch.empty((max(need, 4),), dtype=torch.uint8, device=dev)
+    if out is None:
+        out = alloc_sorted_routes(tokens, topk, experts, dev)
+    with torch.cuda.device(dev):
+        rc = lib.lumen_b200_moe_sort_routes(
+            topk_ids.data_ptr(), topk_weights.data_ptr(), out.sorted_token_ids.data_ptr(),
+            out.sorted_weights.data_ptr(), out.sorted_expert_ids.data_ptr(),
+            out.num_valid_ids.data_ptr(), out.expert_offsets.data_ptr(),
+            out.expert_counts.data_ptr(), out.route_pos.data_ptr(), scratch.data_ptr(),
+            scratch.numel(), tokens, experts, topk, _stream(dev))
+    _cabi.check("lumen_b200_moe_sort_routes", rc)
+    return out
+
+
+def permute_rows(x: torch.Tensor, routes: SortedRoutes, out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _need_cuda(x)
+    T, H = x.shape
+    P = routes.sorted_token_ids.numel()
+    if out is None:
+        out = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        rc = _cabi.load().lumen_b200_moe_permute_rows(
+            x.data_ptr(), routes.sorted_token_ids.data_ptr(), routes.num_valid_ids.data_ptr(),
+            out.data_ptr(), T, H, P, _stream(dev))
+    _cabi.check("lumen_b200_moe_permute_rows", rc)
+    return out
+
+
+def grouped_gemm(acts: torch.Tensor, weights: torch.Tensor, routes: SortedRoutes, *, gated: bool,
+                 rows_hint: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-expert GEMM over rows in expert order; `weights` is [E, (2)N, K]."""
+    dev = _need_cuda(acts, weights)
+    P, K = acts.shape
+    E, w_rows, K2 = weights.shape
+    if K2 != K:
+        raise ValueError(f"weights K ({K2}) must equal activations K ({K}).")
+    N = w_rows // 2 if gated else w_rows
+    if out is None:
+        out = torch.empty((P, N), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        rc = _cabi.load().lumen_b200_moe_grouped_gemm(
+            acts.data_ptr(), weights.data_ptr(), out.data_ptr(), routes.expert_offsets.data_ptr(),
+            routes.expert_counts.data_ptr(), P, E, N, K, 1 if gated else 0, int(rows_hint),
+            _stream(dev))
+    _cabi.check("lumen_b200_moe_grouped_gemm", rc)
+    return out
+
+
+def combine(y: torch.Tensor, routes: SortedRoutes, topk_weights: torch.Tensor, tokens: int,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _need_cuda(y, topk_weights)
+    H = y.shape[1]
+    k = topk_weights.shape[1]
+    if out is None:
+        out = torch.empty((tokens, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        rc = _cabi.load().lumen_b200_moe_combine(
+            y.data_ptr(), routes.route_pos.data_ptr(), topk_weights.data_ptr(), out.data_ptr(),
+            tokens, H, k, _stream(dev))
+    _cabi.check("lumen_b200_moe_combine", rc)
+    return out
+
+
+class FusedMoE:
+    """Pre-allocated buffers + the launch sequence of one MoE forward shape.
+
+    forward_routed(x, topk_ids, topk_weights) takes precomputed routing (the reference
+    harness contract); forward(x, logits=...) / forward(x, w_router=...) runs the in-op
+    router first.  w13 is [E, 2I, H] (gate rows first, up rows second: the w1_q layout of
+    scripts/benchmark/backend_moe.py:162-171), w2 is [E, H, I].
+    """
+
+    def __init__(self, *, tokens: int, hidden: int, inter: int, experts: int, topk: int,
+                 device: torch.device):
+        self.T, self.H, self.I, self.E, self.k = tokens, hidden, inter, experts, topk
+        self.device = device
+        P = max_padded_routes(tokens, topk, experts)
+        self.routes = alloc_sorted_routes(tokens, topk, experts, device)
+        need = int(_cabi.load().lumen_b200_moe_sort_scratch_bytes(tokens, experts, topk))
+        self.scratch = torch.empty((max(need, 4),), dtype=torch.uint8, device=device)
+        self.logits = torch.empty((tokens, experts), dtype=torch.float32, device=device)
+        self.topk_ids = torch.empty((tokens, topk), dtype=torch.int32, device=device)
+        self.topk_weights = torch.empty((tokens, topk), dtype=torch.float32, device=device)
+        self.xs = torch.empty((P, hidden), dtype=torch.bfloat16, device=device)
+        self.h = torch.empty((P, inter), dtype=torch.bfloat16, device=device)
+        self.y = torch.empty((P, hidden), dtype=torch.bfloat16, device=device)
+        self.out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=device)
+        self.rows_hint = max(1, (tokens * topk + experts - 1) // experts)
+
+    def forward_routed(self, x, topk_ids, topk_weights, w13, w2):
+        build_sorted_routes(topk_ids=topk_ids, topk_weights=topk_weights, experts=self.E,
+                            out=self.routes, scratch=self.scratch)
+        permute_rows(x, self.routes, out=self.xs)
+        grouped_gemm(self.xs, w13, self.routes, gated=True, rows_hint=self.rows_hint, out=self.h)
+        grouped_gemm(self.h, w2, self.routes, gated=False, rows_hint=self.rows_hint, out=self.y)
+        return combine(self.y, self.routes, topk_weights, self.T, out=self.out)
+
+    def forward(self, x, w13, w2, *, w_router=None, logits=None):
+        if (w_router is None) == (logits is None):
+            raise ValueError("give exactly one of w_router (in-op router) or logits")
+        if w_router is not None:
+            logits = router_logits(x, w_router, out=self.logits)
+        route_topk(logits, self.k, ids_out=self.topk_ids, weights_out=self.topk_weights)
+        return self.forward_routed(x, self.topk_ids, self.topk_weights, w13, w2)
