@@ -1,0 +1,69 @@
+"""B200 system for datasets/inference/gemm: C[M,N] = A[M,K] * B[N,K]^T in bf16.
+
+Loaded by the reference harness like any other system directory
+(scripts/benchmark/backends.py:95-143 looks for ModelNew, then Model, then
+kernel_function; scripts/benchmark/backend_gemm.py:100-103 uses build_call when present):
+
+    python scripts/benchmark/bench_gemm.py --backend lumen \
+        --model-path <this file> --check-correctness
+"""
+from __future__ import annotations
+
+import importlib.util
+from pathlib import Path
+
+import torch
+import torch.nn as nn
+
+_spec = importlib.util.spec_from_file_location(
+    "_b200_dataset_loader", Path(__file__).resolve().parents[2] / "_loader.py")
+_loader = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(_loader)
+_pkg = _loader.load_b200_package()
+
+kernel_function = _pkg.gemm_pipeline_transposed_b
+
+
+class ModelNew(nn.Module):
+    """forward(a_mk [M,K], b_nk [N,K]) -> [M,N], same dtype (bf16), fp32 accumulation."""
+
+    def __init__(self):
+        super().__init__()
+        self._out_cache: dict = {}
+
+    def build_call(self, *, a_mk: torch.Tensor, b_nk: torch.Tensor):
+        """Zero-argument closure for CUDA-graph capture: the output buffer is allocated
+        here, once, so that replays write to a fixed address."""
+        key = (a_mk.shape[0], b_nk.shape[0], a_mk.device)
+        out = self._out_cache.get(key)
+        if out is None:
+            out = torch.empty((a_mk.shape[0], b_nk.shape[0]), dtype=torch.bfloat16, device=a_mk.device)
+            self._out_cache[key] = out
+        # first call outside capture: sizes the split-K scratch for this shape
+        kernel_function(a_mk, b_nk, out)
+        return lambda: kernel_function(a_mk, b_nk, out)
+
+    def forward(self, a_mk: torch.Tensor, b_nk: torch.Tensor) -> torch.Tensor:
+        return kernel_function(a_mk, b_nk)
+
+
+Model = ModelNew
+
+M = 4096
+K = 4096
+N = 4096
+
+
+def get_inputs():
+    """Seeded stand-ins with the harness' distribution (A, B ~ N(0,1), bf16)."""
+    g = torch.Generator().manual_seed(20260312)
+    a = torch.randn((M, K), generator=g, dtype=torch.float32).to(torch.bfloat16)
+    b = torch.randn((N, K), generator=g, dtype=torch.float32).to(torch.bfloat16)
+    return [a, b]
+
+
+def get_init_inputs():
+    return []
+
+
+__all__ = ["ModelNew", "Model", "kernel_function", "get_inputs", "get_init_inputs"]

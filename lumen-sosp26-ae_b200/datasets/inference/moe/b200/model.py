@@ -1,0 +1,147 @@
+"""B200 system for datasets/inference/moe: fused MoE forward in bf16.
+
+    python scripts/benchmark/bench_moe.py --backend lumen --input-dtype bf16 \
+        --model-path <this file> --check-correctness
+
+`Model(variant=...).build_cases(...)` follows the case-backend contract
+(scripts/benchmark/backend_moe.py:263-336): it receives the harness' precomputed routing
+(topk_ids, topk_weights) and returns zero-argument callables.  `ModelNew.forward` follows
+the python-backend contract (:339-403).  The harness' block scales (input_scale,
+fc1_scale, fc2_scale) are folded into bf16 copies of the activations and weights once,
+outside the timed call, the way the reference's Lumen system pre-shuffles its weights
+(datasets/inference/moe/lumen/model.py:184-199); with unit scales nothing is copied.
+"""
+from __future__ import annotations
+
+import importlib.util
+from pathlib import Path
+from typing import Any, Callable, List
+
+import torch
+import torch.nn as nn
+
+_spec = importlib.util.spec_from_file_location(
+    "_b200_dataset_loader", Path(__file__).resolve().parents[2] / "_loader.py")
+_loader = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(_loader)
+_pkg = _loader.load_b200_package()
+_moe = _pkg.moe
+
+BLOCK = 128
+
+
+def _fold_block_scale(w: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """w [E, rows, cols] bf16 times scale [E, (rows/128)*(cols/128)] -> bf16."""
+    if bool(torch.all(scale == 1.0)):
+        return w
+    E, rows, cols = w.shape
+    s = scale.to(torch.float32).view(E, rows // BLOCK, 1, cols // BLOCK, 1)
+    wf = w.to(torch.float32).view(E, rows // BLOCK, BLOCK, cols // BLOCK, BLOCK) * s
+    return wf.view(E, rows, cols).to(torch.bfloat16).contiguous()
+
+
+def _fold_input_scale(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    if bool(torch.all(scale == 1.0)):
+        return x
+    T, H = x.shape
+    xf = x.to(torch.float32).view(T, H // BLOCK, BLOCK) * scale.to(torch.float32).unsqueeze(-1)
+    return xf.view(T, H).to(torch.bfloat16).contiguous()
+
+
+class Model:
+    def __init__(self, *, variant: str = "b200"):
+        self.variant = variant
+        self._out_cache: dict = {}
+        self._ops: dict = {}
+        self._weight_source = None
+        self._weights = None
+
+    def _prepare_weights(self, w: dict[str, torch.Tensor]):
+        source = (w["w1_q"], w["w2_q"])
+        if self._weights is None or source[0] is not self._weight_source[0] or source[1] is not self._weight_source[1]:
+            self._weights = (_fold_block_scale(w["w1_q"], w["fc1_scale"]),
+                             _fold_block_scale(w["w2_q"], w["fc2_scale"]))
+            self._weight_source = source
+        return self._weights
+
+    def build_cases(self, *, seq_len: int, shared_input: Any, shared_weights: dict[str, torch.Tensor],
+                    dim: int, inter_dim: int, experts: int, topk: int,
+                    input_dtype: str) -> List[Callable[[], torch.Tensor]]:
+        if input_dtype != "bf16":
+            raise ValueError("B200 MoE supports only bf16 input")
+        x = shared_input
+        for name in ("input_q", "topk_weights", "topk_ids", "input_scale"):
+            if not hasattr(x, name):
+                raise ValueError(f"shared_input missing field: {name}")
+        if tuple(x.input_q.shape) != (seq_len, dim):
+            raise ValueError(f"input_q shape mismatch: expected {(seq_len, dim)}, got {tuple(x.input_q.shape)}")
+        if tuple(x.topk_ids.shape) != (seq_len, topk):
+            raise ValueError(f"topk_ids shape mismatch: expected {(seq_len, topk)}, got {tuple(x.topk_ids.shape)}")
+        w13, w2 = self._prepare_weights(shared_weights)
+        if tuple(w13.shape) != (experts, inter_dim * 2, dim):
+            raise ValueError(f"w1_q shape mismatch: expected {(experts, inter_dim * 2, dim)}, got {tuple(w13.shape)}")
+        xin = _fold_input_scale(x.input_q, x.input_scale)
+        dev = xin.device
+        key = (seq_len, dim, inter_dim, experts, topk, dev)
+        op = self._ops.get(key)
+        if op is None:
+            op = _moe.FusedMoE(tokens=seq_len, hidden=dim, inter=inter_dim, experts=experts, topk=topk, device=dev)
+            self._ops[key] = op
+        self._out_cache[key] = op.out
+        ids = x.topk_ids.to(torch.int32).contiguous()
+        wts = x.topk_weights.to(torch.float32).contiguous()
+
+        def run_b200() -> torch.Tensor:
+            return op.forward_routed(xin, ids, wts, w13, w2)
+
+        return [run_b200]
+
+
+class ModelNew(nn.Module):
+    """forward(input_q, w1_q, w2_q, topk_weights, topk_ids, input_scale, fc1_scale, fc2_scale)."""
+
+    def __init__(self):
+        super().__init__()
+        self._impl = Model(variant="b200")
+
+    def forward(self, input_q, w1_q, w2_q, topk_weights, topk_ids, input_scale, fc1_scale, fc2_scale):
+        class _In:
+            pass
+
+        s = _In()
+        s.input_q, s.topk_weights, s.topk_ids, s.input_scale = input_q, topk_weights, topk_ids, input_scale
+        T, H = input_q.shape
+        E, two_i, _ = w1_q.shape
+        weights = {"w1_q": w1_q, "w2_q": w2_q, "fc1_scale": fc1_scale, "fc2_scale": fc2_scale}
+        return self._impl.build_cases(seq_len=T, shared_input=s, shared_weights=weights, dim=H,
+                                      inter_dim=two_i // 2, experts=E, topk=topk_ids.shape[1],
+                                      input_dtype="bf16")[0]()
+
+
+DIM = 4096
+INTER_DIM = 14336
+EXPERTS = 8
+TOPK = 2
+TOKENS = 4096
+SEED = 20260319
+
+
+def get_inputs():
+    """Mixtral-like stand-in inputs (x ~ N(0,1), weights ~ N(0,0.02), unit block scales)."""
+    g = torch.Generator().manual_seed(SEED)
+    x = torch.randn((TOKENS, DIM), generator=g, dtype=torch.float32).to(torch.bfloat16)
+    scores = torch.randn((TOKENS, EXPERTS), generator=g, dtype=torch.float32)
+    tv, ti = torch.topk(scores, k=TOPK, dim=-1, largest=True, sorted=True)
+    gw = torch.Generator().manual_seed(SEED + 17)
+    w1 = (torch.randn((EXPERTS, 2 * INTER_DIM, DIM), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn((EXPERTS, DIM, INTER_DIM), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    ones = lambda *s: torch.ones(s, dtype=torch.float32)  # noqa: E731
+    return [x, w1, w2, torch.softmax(tv, dim=-1), ti.to(torch.int32), ones(TOKENS, DIM // BLOCK),
+            ones(EXPERTS, (2 * INTER_DIM // BLOCK) * (DIM // BLOCK)), ones(EXPERTS, (DIM // BLOCK) * (INTER_DIM // BLOCK))]
+
+
+def get_init_inputs():
+    return []
+
+
+__all__ = ["Model", "ModelNew", "get_inputs", "get_init_inputs"]

@@ -85,8 +85,8 @@ def test_config1_full_size_rows_and_linearity(cuda_pkg):
     c1 = run_gemm(cuda_pkg, a1, bi).float()
     c2 = run_gemm(cuda_pkg, a2, bi).float()
     c12 = run_gemm(cuda_pkg, (a1 + a2), bi).float()
-    # |entries| <= 4 * 4096 * 1 fits bf16's 8 bits only up to 256; compare where exact
-    exact = (c1.abs() <= 256) & (c2.abs() <= 256) & (c12.abs() <= 256)
+    # |entries| <= 4 * 4096 * 1 is exact in bf16 only below 256 (257 already rounds); compare where exact
+    exact = (c1.abs() < 256) & (c2.abs() < 256) & (c12.abs() < 256)
     assert exact.float().mean() > 0.5
     assert torch.equal((c1 + c2)[exact], c12[exact])
 
