@@ -31,6 +31,7 @@ extern "C" {
 #define LUMEN_B200_ECUDA (-3)        /* the CUDA runtime or driver refused a call */
 #define LUMEN_B200_EUNSUPPORTED (-4) /* shape outside what the kernels cover */
 #define LUMEN_B200_EDEVICE (-5)      /* a kernel recorded a wait that gave up */
+#define LUMEN_B200_ESCRATCH_LIMIT (-6) /* shape needs more than the built-in scratch array holds */
 
 /* Library identification, e.g. "lumen_b200 0.1 sm_100a".  Host pointer, static storage. */
 const char* lumen_b200_version(void);
@@ -69,6 +70,30 @@ int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, int M, int N,
  * (0 when the shape does not split).  Counterpart of the 32 MiB plan workspace at
  * datasets/inference/gemm/hipblaslt/hipblaslt_internal_ext.cpp:12,110. */
 size_t lumen_b200_gemm_workspace_bytes(int M, int N, int K);
+
+/* Same result as lumen_b200_gemm_bf16_nt for M <= 128, for callers that cannot give the
+ * library a scratch buffer because they are not allowed to allocate device memory: code
+ * that runs while a stream is being captured, plugins whose host passes them nothing
+ * but their input and output tensors, processes whose memory was carved up at start-up.
+ * The split-K scratch is a 16 MiB array inside the library image (see
+ * lumen_b200_gemm_static_scratch_limit); each GPU that loads the library holds it until
+ * the process exits.  The call allocates and frees nothing.
+ *   - A shape whose split-K plan needs more than the array holds is refused with
+ *     LUMEN_B200_ESCRATCH_LIMIT; M > 128 is refused with LUMEN_B200_EUNSUPPORTED (that
+ *     path needs no scratch: use lumen_b200_gemm_bf16_nt with workspace == NULL).
+ *   - The first call on a device looks up the array's device address and sets kernel
+ *     attributes; make that first call before any stream capture begins.
+ *   - All calls on one device share the one array, and it keeps whatever the previous
+ *     call left there; the part that must start at zero is cleared on `stream` by the
+ *     call itself.  Two calls whose kernels can overlap on the GPU (different streams)
+ *     race on the array: serialise them.
+ * This entry point has no counterpart in the reference. */
+int lumen_b200_gemm_bf16_nt_static(const void* A, const void* B, void* C, int M, int N, int K,
+                                   int lda, int ldb, int ldc, void* stream);
+
+/* Size in bytes of the built-in scratch array used by lumen_b200_gemm_bf16_nt_static.
+ * No counterpart in the reference. */
+size_t lumen_b200_gemm_static_scratch_limit(void);
 
 /* ------------------------------------------------------------- attention -- */
 

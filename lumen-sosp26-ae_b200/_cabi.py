@@ -17,6 +17,7 @@ EWORKSPACE = -2
 ECUDA = -3
 EUNSUPPORTED = -4
 EDEVICE = -5
+ESCRATCH_LIMIT = -6
 
 ERROR_NAMES = {
     EINVAL: "LUMEN_B200_EINVAL (bad pointer, size or pitch)",
@@ -24,6 +25,7 @@ ERROR_NAMES = {
     ECUDA: "LUMEN_B200_ECUDA (CUDA runtime/driver error)",
     EUNSUPPORTED: "LUMEN_B200_EUNSUPPORTED (shape not covered)",
     EDEVICE: "LUMEN_B200_EDEVICE (a kernel wait gave up)",
+    ESCRATCH_LIMIT: "LUMEN_B200_ESCRATCH_LIMIT (shape exceeds the built-in scratch array)",
 }
 
 # name -> (restype, argtypes); mirrors include/lumen_b200.h
@@ -38,6 +40,9 @@ SIGNATURES = {
          c_void_p],
     ),
     "lumen_b200_gemm_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "lumen_b200_gemm_bf16_nt_static": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "lumen_b200_gemm_static_scratch_limit": (c_size_t, []),
     "lumen_b200_fa_fwd_bf16": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int,

@@ -190,3 +190,93 @@ extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights
       return launch_gemm<64, 8, true, false, true>(mp, mq, args, grid, st);
   }
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the weight-streaming (M <= 128) GEMM.
+//
+// Some callers cannot hand this library a scratch buffer because they may not call
+// cudaMalloc at all: code running inside a stream capture, plugins whose host hands
+// them only their input and output tensors, and processes whose memory pool was sized
+// up front and is closed to later requests.  For them the split-K scratch of the
+// M <= 128 path lives in the library image itself, as a fixed array in device memory
+// that every GPU loading the library keeps until the process exits.
+// ---------------------------------------------------------------------------
+namespace b200 {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per GPU
+
+// Device storage.  In host code this name is only a handle for the runtime: it is not
+// a device address, so it is never passed to a kernel; the address is looked up below.
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device, looked up once per device
+// with that device current.  Returns nullptr if the runtime refuses.
+unsigned char* static_scratch_ptr() {
+  static unsigned char* ptrs[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    unsigned char* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_static_scratch) != cudaSuccess)
+      return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" size_t lumen_b200_gemm_static_scratch_limit(void) { return kStaticScratchBytes; }
+
+extern "C" int lumen_b200_gemm_bf16_nt_static(const void* A, const void* B, void* C, int M, int N,
+                                               int K, int lda, int ldb, int ldc, void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LUMEN_B200_EINVAL;
+  if (M > 128) return LUMEN_B200_EUNSUPPORTED;  // larger M uses no scratch: call the plain entry point
+  if (lda < K || ldb < K || ldc < N) return LUMEN_B200_EINVAL;
+  if (lda % 8 != 0 || ldb % 8 != 0) return LUMEN_B200_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return LUMEN_B200_EINVAL;
+  const int sms = device_sm_count();
+  int* status = device_status_word();
+  if (sms <= 0 || !status) return LUMEN_B200_ECUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const SwapPlan plan = plan_swap(M, N, K, sms);
+  const size_t need = plan.splits > 1 ? plan.counter_bytes + plan.partial_bytes : 0;
+  if (need > kStaticScratchBytes) return LUMEN_B200_ESCRATCH_LIMIT;
+
+  GemmArgs args{};
+  args.out = static_cast<__nv_bfloat16*>(C);
+  args.ldo = ldc;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.splits = plan.splits;
+  args.status = status;
+  if (plan.splits > 1) {
+    unsigned char* scratch = static_scratch_ptr();
+    if (!scratch) return LUMEN_B200_ECUDA;
+    args.counters = reinterpret_cast<int*>(scratch);
+    args.ws = reinterpret_cast<float*>(scratch + plan.counter_bytes);
+    // the arrival counters must start at zero; the partial tiles are fully rewritten
+    if (cudaMemsetAsync(args.counters, 0, plan.counter_bytes, st) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+  }
+  CUtensorMap mp, mq;
+  if (encode_tmap_bf16_2d(&mp, B, N, K, ldb, kBlockP) != 0) return LUMEN_B200_ECUDA;
+  if (encode_tmap_bf16_2d(&mq, A, M, K, lda, plan.bn) != 0) return LUMEN_B200_ECUDA;
+  const int units = plan.tiles * plan.splits;
+  const int grid = units < sms ? units : sms;
+  switch (plan.bn) {
+    case 16:
+      return launch_gemm<16, 10, true, false, false>(mp, mq, args, grid, st);
+    case 32:
+      return launch_gemm<32, 10, true, false, false>(mp, mq, args, grid, st);
+    case 64:
+      return launch_gemm<64, 8, true, false, false>(mp, mq, args, grid, st);
+    default:
+      return launch_gemm<128, 6, true, false, false>(mp, mq, args, grid, st);
+  }
+}
