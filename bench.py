@@ -356,6 +356,113 @@ def run_b200_arm(args) -> None:
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- single cases
+def run_case(args) -> None:
+    """One operator case on one GPU, e.g. for profiling or for the per-configuration numbers:
+         --case gemm:MxNxK | c1
+         --case fa:BxSxHqxHkvx{causal|full} | c3a | c3b
+         --case moe:TxHxIxExK[xrouter] | c4 | c5_t1 | c5_t64 | c5_t512 | c5_t8192
+    Prints one JSON line with the device time per call (CUDA events, L2 flushed between calls)."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    entry.build()
+    pkg = importlib.import_module(entry.PACKAGE_NAME)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    pkg.clear_status()
+    peaks = load_peaks()
+    presets = {
+        "c1": "gemm:4096x4096x4096", "c3a": "fa:8x4096x32x8xcausal", "c3b": "fa:2x16384x16x16xfull",
+        "c4": "moe:4096x4096x14336x8x2xrouter", "c5_t1": "moe:1x7168x2048x256x8",
+        "c5_t64": "moe:64x7168x2048x256x8", "c5_t512": "moe:512x7168x2048x256x8",
+        "c5_t8192": "moe:8192x7168x2048x256x8",
+    }
+    case = presets.get(args.case, args.case)
+    kind, _, dims = case.partition(":")
+    parts = dims.split("x")
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    stages = None
+
+    def randn_bf16(shape, std=1.0):
+        return (torch.randn(shape, device=dev, dtype=torch.float32, generator=g) * std).to(torch.bfloat16)
+
+    if kind == "gemm":
+        m, n, k = (int(x) for x in parts)
+        a, b = randn_bf16((m, k)), randn_bf16((n, k), 0.02)
+        out = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+        call = lambda: pkg.gemm_pipeline_transposed_b(a, b, out)  # noqa: E731
+        fl, by = 2.0 * m * n * k, 2.0 * (m * k + n * k + m * n)
+        launches = 1
+    elif kind == "fa":
+        B, S, Hq, Hkv = (int(x) for x in parts[:4])
+        causal = parts[4] == "causal"
+        q, kk, v = randn_bf16((B, S, Hq, 128)), randn_bf16((B, S, Hkv, 128)), randn_bf16((B, S, Hkv, 128))
+        out = torch.empty_like(q)
+        call = lambda: pkg.flash_attn(q, kk, v, causal=causal, out=out)  # noqa: E731
+        fl = 2.0 * B * Hq * S * (S + 1) * 128 if causal else 4.0 * B * Hq * S * S * 128
+        by = 2.0 * B * S * 128 * (2 * Hq + 2 * Hkv)
+        launches = 1
+    elif kind == "moe":
+        T, H, I, E, K = (int(x) for x in parts[:5])
+        router = len(parts) > 5 and parts[5] == "router"
+        x = randn_bf16((T, H))
+        w13 = torch.empty((E, 2 * I, H), device=dev, dtype=torch.bfloat16)
+        w2 = torch.empty((E, H, I), device=dev, dtype=torch.bfloat16)
+        for e in range(E):  # per expert: keeps the fp32 temporaries small
+            w13[e] = randn_bf16((2 * I, H), 0.02)
+            w2[e] = randn_bf16((H, I), 0.02)
+        w_router = randn_bf16((E, H), 0.02) if router else None
+        logits = None if router else torch.randn((T, E), device=dev, dtype=torch.float32, generator=g)
+        op = pkg.moe.FusedMoE(tokens=T, hidden=H, inter=I, experts=E, topk=K, device=dev)
+        call = lambda: op.forward(x, w13, w2, w_router=w_router, logits=logits)  # noqa: E731
+        call()
+        torch.cuda.synchronize()
+        touched = int((op.routes.expert_counts > 0).sum().item())
+        fl = 6.0 * T * K * H * I + (2.0 * T * H * E if router else 0.0)
+        by = 3.0 * H * I * 2 * touched + 2.0 * T * H * 2
+        launches = 8 if router else 7
+        stages = op.stage_times(x, w13, w2, w_router=w_router, logits=logits)
+    else:
+        raise SystemExit(f"unknown case {args.case!r}")
+
+    for _ in range(max(args.warmup, 1)):
+        call()
+    torch.cuda.synchronize()
+    # like the reference's timer (scripts/benchmark/cudagraph_timer.py:33-55): capture the
+    # call in a CUDA graph and time replays, so host launch gaps are not counted
+    run = call
+    if not args.eager:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            call()
+        torch.cuda.synchronize()
+        run = graph.replay
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    status = pkg.device_status()
+    line = {
+        "case": case, "ms": ms, "ms_min": min(times), "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6,
+        "frac_tensor_peak": fl / ms / 1e9 / peaks["bf16_tflops"], "frac_hbm_peak": by / ms / 1e6 / peaks["hbm_gbs"],
+        "peak_source": peaks["source"], "algorithmic_flop": fl, "algorithmic_bytes": by, "steps": args.steps,
+        "launches_per_call": launches, "l2": "flushed between calls (256 MB write)", "status": status,
+        "timing": "eager launches" if args.eager else "CUDA graph replay",
+    }
+    if stages:
+        line["stage_ms"] = stages
+    print(json.dumps(line), flush=True)
+
+
 # DRAM bytes per launch of the dominant kernel from the ncu capture summarised under
 # profiles/ (null until a capture exists for the current kernel).
 TRAFFIC_BYTES_PER_LAUNCH = None
@@ -367,8 +474,12 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--eager", action="store_true", help="--case: time eager launches instead of graph replays")
+    ap.add_argument("--case", default=None, help="run one operator case instead of the sweep (see run_case)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_b200_arm(args)

@@ -56,7 +56,9 @@ int lumen_b200_clear_status(void);
  * to nearest even.  Row-major with pitches lda, ldb, ldc in elements; lda and ldb
  * must be multiples of 8 and A, B 16-byte aligned.  M <= 128 takes the
  * weight-streaming split-K path, which uses `workspace`; with workspace == NULL
- * that path runs unsplit.
+ * that path runs unsplit.  A new workspace must be zero-filled once by the caller;
+ * every call leaves its first lumen_b200_gemm_workspace_bytes() bytes reusable by the
+ * next call on the same stream (calls that overlap on the GPU need separate workspaces).
  * Replaces gemm_pipeline_transposed_b(A, B, out)
  * (datasets/inference/gemm/lumen/amdgpu_gemm.py:872-923), the ksearch launch
  * wrapper (datasets/inference/gemm/ksearch/kernel.h:7-17) and

@@ -104,3 +104,24 @@ def load(path: Path | None = None) -> ctypes.CDLL:
 def check(fn: str, code: int) -> None:
     if code != OK:
         raise LumenB200Error(fn, code)
+
+
+class _NoSwitch:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_SWITCH = _NoSwitch()
+
+
+def on_device(device):
+    """Context that makes `device` current for a C-ABI call; free when it already is."""
+    import torch
+
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if torch.cuda.current_device() == idx:
+        return _NO_SWITCH
+    return torch.cuda.device(idx)

@@ -55,7 +55,7 @@ def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: boo
         return out
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    with torch.cuda.device(q.device):
+    with _cabi.on_device(q.device):
         rc = _cabi.load().lumen_b200_fa_fwd_bf16(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, S, Hq, Hkv, D,
             float(scale), 1 if causal else 0, torch.cuda.current_stream(q.device).cuda_stream)

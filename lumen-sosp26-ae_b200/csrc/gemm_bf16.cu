@@ -1,6 +1,8 @@
 // Host launchers and C-ABI entry points of the BF16 contraction core: the dense
 // GEMM C = A * B^T and the per-expert (grouped) GEMMs of the MoE.
 #include "gemm_bf16.cuh"
+#include "gemm_bf16_pair.cuh"
+#include <cstdlib>
 #include "lumen_b200_internal.h"
 
 namespace b200 {
@@ -23,6 +25,49 @@ int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& ar
   }
   kern<<<grid, kGemmThreads, smem, st>>>(mp, mq, args);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+// dense GEMM on CTA pairs (clusters of 2); grid = 2 CTAs per co-resident cluster
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int units,
+                     cudaStream_t st) {
+  constexpr int kStages = 6;
+  auto kern = gemm_bf16_pair_kernel<kStages>;
+  constexpr size_t smem = gemm_pair_smem_bytes<kStages>();
+  static_assert(smem <= 227 * 1024, "stage ring does not fit shared memory");
+  static bool configured[64] = {};
+  static int max_clusters[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LUMEN_B200_ECUDA;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = device_sm_count() / 2;
+    }
+    max_clusters[dev] = n;
+    configured[dev] = true;
+  }
+  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  kern<<<2 * clusters, kGemmThreads, smem, st>>>(ma, mb, args);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+// Tile choice for the dense path: "pair" (256 x 256 per CTA pair) unless the environment
+// variable LUMEN_B200_GEMM_TILE says "single" (128 x 256 per CTA).
+bool use_pair_tiles() {
+  static int cached = -1;
+  if (cached < 0) {
+    const char* v = std::getenv("LUMEN_B200_GEMM_TILE");
+    cached = (v && v[0] == 's') ? 0 : 1;
+  }
+  return cached == 1;
 }
 
 inline int ceil_div_h(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
@@ -87,6 +132,13 @@ extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, in
   args.status = status;
 
   CUtensorMap mp, mq;
+  if (M > 128 && use_pair_tiles()) {
+    // CTA pairs: each CTA loads 128-row boxes of A and of B
+    if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
+    if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, kBlockP) != 0) return LUMEN_B200_ECUDA;
+    const int units = ((M + kPairTileM - 1) / kPairTileM) * ((N + kPairTileN - 1) / kPairTileN);
+    return launch_gemm_pair(mp, mq, args, units, st);
+  }
   if (M > 128) {
     // P = A (128-row boxes), Q = B (256-row boxes)
     if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
@@ -108,8 +160,8 @@ extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, in
     args.splits = plan.splits;
     args.counters = static_cast<int*>(workspace);
     args.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + plan.counter_bytes);
-    if (cudaMemsetAsync(args.counters, 0, plan.counter_bytes, st) != cudaSuccess)
-      return LUMEN_B200_ECUDA;
+    // the arrival counters at the head of the workspace are zero on entry (the caller
+    // zero-fills a new workspace once) and the kernel leaves them zero
   }
   if (encode_tmap_bf16_2d(&mp, B, N, K, ldb, kBlockP) != 0) return LUMEN_B200_ECUDA;
   if (encode_tmap_bf16_2d(&mq, A, M, K, lda, plan.bn) != 0) return LUMEN_B200_ECUDA;

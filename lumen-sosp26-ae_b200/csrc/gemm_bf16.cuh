@@ -494,12 +494,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (last) {
             __threadfence();
             const float* base = args.ws + size_t(t.tile_id) * args.splits * (size_t(BN) * kBlockP);
-            for (int r = 0; r < t.rows_valid; ++r) {
-              float acc = 0.f;
-              for (int s = 0; s < args.splits; ++s)
-                acc += __ldcg(base + size_t(s) * (size_t(BN) * kBlockP) + r * kBlockP + p);
-              if (col_ok)
-                args.out[size_t(t.out_row + r) * args.ldo + t.out_col + p] = __float2bfloat16_rn(acc);
+            constexpr int kRowsPerPass = 8;  // independent sums keep 8 x splits loads in flight
+            for (int r0 = 0; r0 < t.rows_valid; r0 += kRowsPerPass) {
+              float acc[kRowsPerPass];
+#pragma unroll
+              for (int i = 0; i < kRowsPerPass; ++i) acc[i] = 0.f;
+              for (int s = 0; s < args.splits; ++s) {
+                const float* slice = base + size_t(s) * (size_t(BN) * kBlockP) + p;
+#pragma unroll
+                for (int i = 0; i < kRowsPerPass; ++i)
+                  if (r0 + i < BN) acc[i] += __ldcg(slice + (r0 + i) * kBlockP);
+              }
+              if (col_ok) {
+#pragma unroll
+                for (int i = 0; i < kRowsPerPass; ++i)
+                  if (r0 + i < t.rows_valid)
+                    args.out[size_t(t.out_row + r0 + i) * args.ldo + t.out_col + p] =
+                        __float2bfloat16_rn(acc[i]);
+              }
             }
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");  // last_flag is reused by the next unit

@@ -74,7 +74,7 @@ def gemm_pipeline_transposed_b(
         raise ValueError("out must be row-major.")
 
     lib = _cabi.load()
-    with torch.cuda.device(A.device):
+    with _cabi.on_device(A.device):
         ws = _workspace(A.device, int(lib.lumen_b200_gemm_workspace_bytes(m, n, k)))
         stream = torch.cuda.current_stream(A.device).cuda_stream
         rc = lib.lumen_b200_gemm_bf16_nt(

@@ -48,7 +48,7 @@ def router_logits(x: torch.Tensor, w_router: torch.Tensor, out: torch.Tensor | N
         raise ValueError(f"w_router must be [E,{H}], got {tuple(w_router.shape)}.")
     if out is None:
         out = torch.empty((T, E), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _cabi.on_device(dev):
         rc = _cabi.load().lumen_b200_moe_router_logits(
             x.data_ptr(), w_router.data_ptr(), out.data_ptr(), T, H, E, _stream(dev))
     _cabi.check("lumen_b200_moe_router_logits", rc)
@@ -67,7 +67,7 @@ def route_topk(logits: torch.Tensor, topk: int,
         raise ValueError(f"topk ({topk}) must be <= experts ({E})")
     ids = ids_out if ids_out is not None else torch.empty((T, topk), dtype=torch.int32, device=dev)
     w = weights_out if weights_out is not None else torch.empty((T, topk), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _cabi.on_device(dev):
         rc = _cabi.load().lumen_b200_moe_route_topk(
             logits.data_ptr(), ids.data_ptr(), w.data_ptr(), T, E, topk, _stream(dev))
     _cabi.check("lumen_b200_moe_route_topk", rc)
@@ -125,7 +125,7 @@ def build_sorted_routes(*, topk_ids: torch.Tensor, topk_weights: torch.Tensor, e
         scratch = torch.empty((max(need, 4),), dtype=torch.uint8, device=dev)
     if out is None:
         out = alloc_sorted_routes(tokens, topk, experts, dev)
-    with torch.cuda.device(dev):
+    with _cabi.on_device(dev):
         rc = lib.lumen_b200_moe_sort_routes(
             topk_ids.data_ptr(), topk_weights.data_ptr(), out.sorted_token_ids.data_ptr(),
             out.sorted_weights.data_ptr(), out.sorted_expert_ids.data_ptr(),
@@ -142,7 +142,7 @@ def permute_rows(x: torch.Tensor, routes: SortedRoutes, out: torch.Tensor | None
     P = routes.sorted_token_ids.numel()
     if out is None:
         out = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _cabi.on_device(dev):
         rc = _cabi.load().lumen_b200_moe_permute_rows(
             x.data_ptr(), routes.sorted_token_ids.data_ptr(), routes.num_valid_ids.data_ptr(),
             out.data_ptr(), T, H, P, _stream(dev))
@@ -161,7 +161,7 @@ def grouped_gemm(acts: torch.Tensor, weights: torch.Tensor, routes: SortedRoutes
     N = w_rows // 2 if gated else w_rows
     if out is None:
         out = torch.empty((P, N), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _cabi.on_device(dev):
         rc = _cabi.load().lumen_b200_moe_grouped_gemm(
             acts.data_ptr(), weights.data_ptr(), out.data_ptr(), routes.expert_offsets.data_ptr(),
             routes.expert_counts.data_ptr(), P, E, N, K, 1 if gated else 0, int(rows_hint),
@@ -177,7 +177,7 @@ def combine(y: torch.Tensor, routes: SortedRoutes, topk_weights: torch.Tensor, t
     k = topk_weights.shape[1]
     if out is None:
         out = torch.empty((tokens, H), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _cabi.on_device(dev):
         rc = _cabi.load().lumen_b200_moe_combine(
             y.data_ptr(), routes.route_pos.data_ptr(), topk_weights.data_ptr(), out.data_ptr(),
             tokens, H, k, _stream(dev))
@@ -226,3 +226,40 @@ class FusedMoE:
             logits = router_logits(x, w_router, out=self.logits)
         route_topk(logits, self.k, ids_out=self.topk_ids, weights_out=self.topk_weights)
         return self.forward_routed(x, self.topk_ids, self.topk_weights, w13, w2)
+
+    def stage_times(self, x, w13, w2, *, w_router=None, logits=None, repeats: int = 5) -> dict:
+        """Median device time (ms) of each launch group of one forward, from CUDA events
+        on the current stream.  Measurement helper; not used by forward()."""
+        import statistics
+
+        def timed(fn):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            return (e0, e1)
+
+        samples: dict[str, list] = {}
+        for _ in range(repeats):
+            ev = {}
+            if w_router is not None:
+                ev["router_logits"] = timed(lambda: router_logits(x, w_router, out=self.logits))
+                lg = self.logits
+            else:
+                lg = logits
+            ev["topk_softmax"] = timed(lambda: route_topk(lg, self.k, ids_out=self.topk_ids,
+                                                          weights_out=self.topk_weights))
+            ev["sort_routes"] = timed(lambda: build_sorted_routes(
+                topk_ids=self.topk_ids, topk_weights=self.topk_weights, experts=self.E,
+                out=self.routes, scratch=self.scratch))
+            ev["permute_rows"] = timed(lambda: permute_rows(x, self.routes, out=self.xs))
+            ev["gemm_w13_silu"] = timed(lambda: grouped_gemm(self.xs, w13, self.routes, gated=True,
+                                                             rows_hint=self.rows_hint, out=self.h))
+            ev["gemm_w2"] = timed(lambda: grouped_gemm(self.h, w2, self.routes, gated=False,
+                                                       rows_hint=self.rows_hint, out=self.y))
+            ev["combine"] = timed(lambda: combine(self.y, self.routes, self.topk_weights, self.T,
+                                                  out=self.out))
+            torch.cuda.synchronize()
+            for name, (e0, e1) in ev.items():
+                samples.setdefault(name, []).append(e0.elapsed_time(e1))
+        return {name: statistics.median(v) for name, v in samples.items()}
