@@ -463,6 +463,73 @@ def run_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_ep_case(args) -> None:
+    """Expert-parallel MoE over all ranks of the job (torchrun): tokens T/G and experts E/G
+    per rank, NCCL all-to-all dispatch and combine.  --case ep:TxHxIxExK or ep:c4 / ep:c5_tN.
+    Rank 0 prints one JSON line; time = max over ranks of the device time per forward."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as entry
+
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", device_id=dev)
+    if rank == 0:
+        entry.build()
+    dist.barrier()
+    pkg = importlib.import_module(entry.PACKAGE_NAME)
+    pkg._cabi.load()
+    pkg.clear_status()
+    presets = {"c4": "4096x4096x14336x8x2", "c5_t1": "1x7168x2048x256x8", "c5_t64": "64x7168x2048x256x8",
+               "c5_t512": "512x7168x2048x256x8", "c5_t8192": "8192x7168x2048x256x8"}
+    dims = args.case.split(":", 1)[1]
+    T, H, I, E, K = (int(x) for x in presets.get(dims, dims).split("x")[:5])
+    if E % world or T % world:
+        raise SystemExit(f"T={T}, E={E} do not split over {world} ranks")
+    Tl, El = T // world, E // world
+    g = torch.Generator(device=dev).manual_seed(SEED + rank)
+
+    def randn_bf16(shape, std=1.0):
+        return (torch.randn(shape, device=dev, dtype=torch.float32, generator=g) * std).to(torch.bfloat16)
+
+    x = randn_bf16((Tl, H))
+    logits = torch.randn((Tl, E), device=dev, dtype=torch.float32, generator=g)
+    w13 = torch.empty((El, 2 * I, H), device=dev, dtype=torch.bfloat16)
+    w2 = torch.empty((El, H, I), device=dev, dtype=torch.bfloat16)
+    for e in range(El):
+        w13[e] = randn_bf16((2 * I, H), 0.02)
+        w2[e] = randn_bf16((H, I), 0.02)
+    ops = pkg.moe_ep.CudaOps(dev, tokens_global=T, experts=E, topk=K)
+    ep = pkg.moe_ep.ExpertParallelMoE(experts=E, topk=K, ops=ops)
+    for _ in range(max(args.warmup, 2)):
+        ep.forward(x, w13, w2, logits=logits)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ep.forward(x, w13, w2, logits=logits)
+    e1.record()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    status = pkg.device_status()
+    if rank == 0:
+        fl = 6.0 * T * K * H * I
+        print(json.dumps({"case": args.case, "n_gpus": world, "ms": ms, "tokens_per_s": T / ms * 1e3,
+                          "tflops": fl / ms / 1e9, "tokens": T, "experts": E, "topk": K,
+                          "parallelism": f"expert-parallel x{world}, tokens {Tl}/rank, experts {El}/rank, NCCL all_to_all",
+                          "timing": "eager (one host read of the per-expert counts per forward)",
+                          "status": status}), flush=True)
+    dist.destroy_process_group()
+
+
 # DRAM bytes per launch of the dominant kernel from the ncu capture summarised under
 # profiles/ (null until a capture exists for the current kernel).
 TRAFFIC_BYTES_PER_LAUNCH = None
@@ -477,7 +544,9 @@ def main() -> None:
     ap.add_argument("--eager", action="store_true", help="--case: time eager launches instead of graph replays")
     ap.add_argument("--case", default=None, help="run one operator case instead of the sweep (see run_case)")
     args = ap.parse_args()
-    if args.case:
+    if args.case and args.case.startswith("ep:"):
+        run_ep_case(args)
+    elif args.case:
         run_case(args)
     elif args.impl == "reference":
         run_reference_arm(args)

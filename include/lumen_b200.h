@@ -126,8 +126,10 @@ int lumen_b200_moe_route_topk(const void* logits, void* topk_ids, void* topk_wei
 
 size_t lumen_b200_moe_sort_scratch_bytes(int T, int E, int k);
 
-/* Stable expert-major sort of the T*k routes.  With P = T*k + E*32 - k and
- * NB = ceil(P / 32):
+/* Stable expert-major sort of the T*k routes.  route_group = 32 gives the reference
+ * layout below; route_group = 1 gives the compact layout (no padding between experts,
+ * sorted_expert_ids may be NULL) that the expert-parallel dispatch sends.  With
+ * P = T*k + E*32 - k and NB = ceil(P / 32):
  *   sorted_token_ids[P]  int32  (slot << 24) | token, pads (k << 24) | T
  *   sorted_weights[P]    fp32   route weight, pads 0
  *   sorted_expert_ids[NB] int32 expert of each block of 32 sorted routes, unused -1
@@ -141,7 +143,8 @@ int lumen_b200_moe_sort_routes(const void* topk_ids, const void* topk_weights,
                                void* sorted_token_ids, void* sorted_weights,
                                void* sorted_expert_ids, void* num_valid_ids, void* expert_offsets,
                                void* expert_counts, void* route_pos, void* scratch,
-                               size_t scratch_bytes, int T, int E, int k, void* stream);
+                               size_t scratch_bytes, int T, int E, int k, int route_group,
+                               void* stream);
 
 /* xs[pos,:] = x[token(sorted_token_ids[pos]),:] for pos < num_valid_ids[0]; pad rows
  * become 0.  max_rows = T*k + E*32 - k bounds the launch.  Replaces the gather in

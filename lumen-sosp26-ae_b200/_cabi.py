@@ -56,7 +56,7 @@ SIGNATURES = {
     "lumen_b200_moe_sort_routes": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-         c_void_p, c_size_t, c_int, c_int, c_int, c_void_p],
+         c_void_p, c_size_t, c_int, c_int, c_int, c_int, c_void_p],
     ),
     "lumen_b200_moe_permute_rows": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),

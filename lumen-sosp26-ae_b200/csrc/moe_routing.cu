@@ -10,7 +10,6 @@
 namespace b200 {
 
 constexpr int kRouteChunk = 1024;  // routes ranked by one CTA
-constexpr int kRouteGroup = 32;    // the reference pads every expert to a multiple of 32 routes
 
 // ---------------------------------------------------------------------------
 // router logits: logits[t][e] = sum_h x[t][h] * wr[e][h]   (bf16 in, fp32 out)
@@ -188,19 +187,22 @@ __global__ void __launch_bounds__(1024)
                     int* __restrict__ expert_offsets, int* __restrict__ expert_counts,
                     int* __restrict__ sorted_token_ids, float* __restrict__ sorted_weights,
                     int* __restrict__ sorted_expert_ids, int* __restrict__ num_valid_ids, int T, int k,
-                    int E, int nchunks) {
+                    int E, int nchunks, int group) {
   __shared__ int s_warp[32];
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
 
-  const int max_padded = T * k + E * kRouteGroup - k;
-  const int max_blocks = (max_padded + kRouteGroup - 1) / kRouteGroup;
+  // `group`: every expert's routes are padded to a multiple of it (32 = the reference
+  // layout with its per-block expert map; 1 = compact, no padding, no block map)
+  const int max_padded = T * k + E * group - k;
+  const int max_blocks = (max_padded + group - 1) / group;
   const int sentinel = (k << 24) | T;
   for (int i = tid; i < max_padded; i += blockDim.x) {
     sorted_token_ids[i] = sentinel;
     sorted_weights[i] = 0.f;
   }
-  for (int i = tid; i < max_blocks; i += blockDim.x) sorted_expert_ids[i] = -1;
+  if (sorted_expert_ids)
+    for (int i = tid; i < max_blocks; i += blockDim.x) sorted_expert_ids[i] = -1;
 
   int carry_all = 0;  // padded routes of the experts handled in earlier rounds
   for (int e0 = 0; e0 < E; e0 += blockDim.x) {
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(1024)
         cnt += v;
       }
     }
-    const int padded = (cnt + kRouteGroup - 1) / kRouteGroup * kRouteGroup;
+    const int padded = (cnt + group - 1) / group * group;
     // block-wide exclusive scan of `padded`
     int incl = padded;
 #pragma unroll
@@ -241,8 +243,8 @@ __global__ void __launch_bounds__(1024)
       expert_counts[e] = cnt;
     }
     __syncthreads();  // the pad fill above is complete before any block id is written
-    if (e < E) {
-      for (int b = off / kRouteGroup; b < (off + padded) / kRouteGroup; ++b) sorted_expert_ids[b] = e;
+    if (e < E && sorted_expert_ids) {
+      for (int b = off / group; b < (off + padded) / group; ++b) sorted_expert_ids[b] = e;
     }
     carry_all += round_total;
     __syncthreads();
@@ -410,10 +412,11 @@ extern "C" int lumen_b200_moe_sort_routes(const void* topk_ids, const void* topk
                                            void* sorted_expert_ids, void* num_valid_ids,
                                            void* expert_offsets, void* expert_counts, void* route_pos,
                                            void* scratch, size_t scratch_bytes, int T, int E, int k,
-                                           void* stream) {
-  if (!topk_ids || !topk_weights || !sorted_token_ids || !sorted_weights || !sorted_expert_ids ||
-      !num_valid_ids || !expert_offsets || !expert_counts || !route_pos || !scratch)
+                                           int route_group, void* stream) {
+  if (!topk_ids || !topk_weights || !sorted_token_ids || !sorted_weights || !num_valid_ids ||
+      !expert_offsets || !expert_counts || !route_pos || !scratch)
     return LUMEN_B200_EINVAL;
+  if (route_group < 1 || (route_group > 1 && !sorted_expert_ids)) return LUMEN_B200_EINVAL;
   // token index must fit the 24-bit field of the packed route id
   if (T <= 0 || E <= 0 || k <= 0 || E > kMaxExperts || T >= (1 << 24) || k > 127)
     return LUMEN_B200_EINVAL;
@@ -429,7 +432,7 @@ extern "C" int lumen_b200_moe_sort_routes(const void* topk_ids, const void* topk
                                       static_cast<int*>(sorted_token_ids),
                                       static_cast<float*>(sorted_weights),
                                       static_cast<int*>(sorted_expert_ids),
-                                      static_cast<int*>(num_valid_ids), T, k, E, nchunks);
+                                      static_cast<int*>(num_valid_ids), T, k, E, nchunks, route_group);
   moe_rank_scatter_kernel<<<nchunks, kRouteChunk, 0, st>>>(
       static_cast<const int*>(topk_ids), static_cast<const float*>(topk_weights), hist,
       static_cast<const int*>(expert_offsets), static_cast<int*>(sorted_token_ids),

@@ -90,13 +90,14 @@ class SortedRoutes:
         return (self.sorted_token_ids, self.sorted_weights, self.sorted_expert_ids, self.num_valid_ids)
 
 
-def max_padded_routes(tokens: int, topk: int, experts: int) -> int:
-    return tokens * topk + experts * ROUTE_GROUP_SIZE - topk
+def max_padded_routes(tokens: int, topk: int, experts: int, group: int = ROUTE_GROUP_SIZE) -> int:
+    return tokens * topk + experts * group - topk
 
 
-def alloc_sorted_routes(tokens: int, topk: int, experts: int, device: torch.device) -> SortedRoutes:
-    P = max_padded_routes(tokens, topk, experts)
-    nb = (P + ROUTE_GROUP_SIZE - 1) // ROUTE_GROUP_SIZE
+def alloc_sorted_routes(tokens: int, topk: int, experts: int, device: torch.device,
+                        group: int = ROUTE_GROUP_SIZE) -> SortedRoutes:
+    P = max_padded_routes(tokens, topk, experts, group)
+    nb = (P + group - 1) // group
     i32 = dict(dtype=torch.int32, device=device)
     return SortedRoutes(
         sorted_token_ids=torch.empty((P,), **i32),
@@ -110,9 +111,10 @@ def alloc_sorted_routes(tokens: int, topk: int, experts: int, device: torch.devi
 
 
 def build_sorted_routes(*, topk_ids: torch.Tensor, topk_weights: torch.Tensor, experts: int,
-                        out: SortedRoutes | None = None,
-                        scratch: torch.Tensor | None = None) -> SortedRoutes:
-    """Device version of _build_sorted_routes (same keyword arguments)."""
+                        out: SortedRoutes | None = None, scratch: torch.Tensor | None = None,
+                        group: int = ROUTE_GROUP_SIZE) -> SortedRoutes:
+    """Device version of _build_sorted_routes (same keyword arguments).  group=32 is the
+    reference layout; group=1 packs the experts back to back (expert-parallel dispatch)."""
     dev = _need_cuda(topk_ids, topk_weights)
     if topk_ids.dtype != torch.int32 or topk_weights.dtype != torch.float32:
         raise ValueError("topk_ids must be int32 and topk_weights float32.")
@@ -124,14 +126,14 @@ def build_sorted_routes(*, topk_ids: torch.Tensor, topk_weights: torch.Tensor, e
     if scratch is None:
         scratch = torch.empty((max(need, 4),), dtype=torch.uint8, device=dev)
     if out is None:
-        out = alloc_sorted_routes(tokens, topk, experts, dev)
+        out = alloc_sorted_routes(tokens, topk, experts, dev, group)
     with _cabi.on_device(dev):
         rc = lib.lumen_b200_moe_sort_routes(
             topk_ids.data_ptr(), topk_weights.data_ptr(), out.sorted_token_ids.data_ptr(),
             out.sorted_weights.data_ptr(), out.sorted_expert_ids.data_ptr(),
             out.num_valid_ids.data_ptr(), out.expert_offsets.data_ptr(),
             out.expert_counts.data_ptr(), out.route_pos.data_ptr(), scratch.data_ptr(),
-            scratch.numel(), tokens, experts, topk, _stream(dev))
+            scratch.numel(), tokens, experts, topk, int(group), _stream(dev))
     _cabi.check("lumen_b200_moe_sort_routes", rc)
     return out
 
@@ -146,6 +148,25 @@ def permute_rows(x: torch.Tensor, routes: SortedRoutes, out: torch.Tensor | None
         rc = _cabi.load().lumen_b200_moe_permute_rows(
             x.data_ptr(), routes.sorted_token_ids.data_ptr(), routes.num_valid_ids.data_ptr(),
             out.data_ptr(), T, H, P, _stream(dev))
+    _cabi.check("lumen_b200_moe_permute_rows", rc)
+    return out
+
+
+def gather_rows(rows: torch.Tensor, index: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[i,:] = rows[index[i],:] (an index >= len(rows) gives a zero row); bf16 rows, int32 index."""
+    dev = _need_cuda(rows, index)
+    if index.dtype != torch.int32 or index.ndim != 1:
+        raise ValueError("index must be a 1-D int32 tensor")
+    R, H = rows.shape
+    n = index.numel()
+    if out is None:
+        out = torch.empty((n, H), dtype=torch.bfloat16, device=dev)
+    if n == 0:
+        return out
+    count = torch.tensor([n, R], dtype=torch.int32, device=dev)
+    with _cabi.on_device(dev):
+        rc = _cabi.load().lumen_b200_moe_permute_rows(
+            rows.data_ptr(), index.data_ptr(), count.data_ptr(), out.data_ptr(), R, H, n, _stream(dev))
     _cabi.check("lumen_b200_moe_permute_rows", rc)
     return out
 

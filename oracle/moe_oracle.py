@@ -40,8 +40,10 @@ def min_topk_gap(logits: torch.Tensor, topk: int) -> float:
     return float(gaps.min())
 
 
-def build_sorted_routes(topk_ids: np.ndarray, topk_weights: np.ndarray, experts: int):
-    """numpy restatement of _build_sorted_routes.  Returns
+def build_sorted_routes(topk_ids: np.ndarray, topk_weights: np.ndarray, experts: int,
+                        group: int = ROUTE_GROUP_SIZE):
+    """numpy restatement of _build_sorted_routes (`group` = its ROUTE_GROUP_SIZE; 1 gives
+    the compact layout without padding between experts).  Returns
     (sorted_token_ids i32 [P], sorted_weights f32 [P], sorted_expert_ids i32 [NB],
      num_valid_ids i32 [2], expert_offsets i32 [E+1], expert_counts i32 [E], route_pos i32 [T*k]);
     the first four are the reference's tuple, the last three are the derived tables the
@@ -49,8 +51,8 @@ def build_sorted_routes(topk_ids: np.ndarray, topk_weights: np.ndarray, experts:
     topk_ids = np.asarray(topk_ids, dtype=np.int32)
     topk_weights = np.asarray(topk_weights, dtype=np.float32)
     tokens, topk = topk_ids.shape
-    P = tokens * topk + experts * ROUTE_GROUP_SIZE - topk
-    NB = (P + ROUTE_GROUP_SIZE - 1) // ROUTE_GROUP_SIZE
+    P = tokens * topk + experts * group - topk
+    NB = (P + group - 1) // group
     sorted_token_ids = np.full((P,), (topk << 24) | tokens, dtype=np.int32)
     sorted_weights = np.zeros((P,), dtype=np.float32)
     sorted_expert_ids = np.full((NB,), -1, dtype=np.int32)
@@ -69,9 +71,9 @@ def build_sorted_routes(topk_ids: np.ndarray, topk_weights: np.ndarray, experts:
         sorted_token_ids[begin:begin + n] = (slot.astype(np.int32) << 24) | tok.astype(np.int32)
         sorted_weights[begin:begin + n] = topk_weights[tok, slot]
         route_pos[tok * topk + slot] = begin + np.arange(n, dtype=np.int32)
-        nblk = (n + ROUTE_GROUP_SIZE - 1) // ROUTE_GROUP_SIZE
+        nblk = (n + group - 1) // group
         sorted_expert_ids[blk:blk + nblk] = e
-        begin += nblk * ROUTE_GROUP_SIZE
+        begin += nblk * group
         blk += nblk
     expert_offsets[experts] = begin
     num_valid_ids = np.array([begin, tokens], dtype=np.int32)
