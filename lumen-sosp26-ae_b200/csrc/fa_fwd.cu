@@ -30,7 +30,12 @@ constexpr int kFaTile = 128;     // query rows per tile and keys per KV tile
 constexpr int kFaD = 128;        // head dimension
 constexpr int kFaHalfBytes = kFaTile * 64 * 2;   // one [128][64] bf16 swizzled panel
 constexpr int kFaTileBytes = 2 * kFaHalfBytes;   // one [128][128] tile = two panels
+constexpr int kFaRegsCopy = 72;      // registers per thread kept by the copy/MMA warpgroup
+constexpr int kFaRegsSoftmax = 216;  // registers per thread taken by the softmax warpgroups
+static_assert(128 * kFaRegsCopy + 256 * kFaRegsSoftmax <= 384 * 168, "register file budget");
 constexpr float kLazyRescaleLog2 = 8.0f;
+// evaluate every fourth exp2 with the FMA-pipe polynomial instead of the MUFU
+constexpr bool kExp2OnFmaPipe = false;
 
 enum FaWaitCode {
   kFaWaitQ = 16,
@@ -130,8 +135,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem_base = tail->tmem_slot;
 
+  // 384 threads x 168 registers at launch: the copy/MMA warpgroup keeps 56 per thread, the
+  // two softmax warpgroups take 224 (they hold a 128-wide score row per thread)
+  // (each role branch below starts with its own setmaxnreg so that the register bound of
+  // a branch is visible to the compiler)
   if (warp == 0) {
     // ================================ TMA producer ======================================
+    reg_dealloc<kFaRegsCopy>();
     if (lane == 0) {
       const uint32_t qbar = smem_u32(&tail->q_full);
       const int active = (n_tiles[0] > 0 ? 1 : 0) + (n_tiles[1] > 0 ? 1 : 0);
@@ -161,6 +171,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
   } else if (warp == 1) {
     // ================================ MMA issuer ========================================
+    reg_dealloc<kFaRegsCopy>();
     if (lane == 0) {
       // S = Q K^T: both operands K-major (rows of 128 d-elements as two 64-wide panels)
       constexpr uint32_t idesc_qk = make_idesc_bf16(128, 128, 0, 0);
@@ -241,8 +252,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (j + 1 < n_max) umma_commit(smem_u32(&tail->kv_empty[kseq % SLOTS]));
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    reg_dealloc<kFaRegsCopy>();
+  } else {
     // ================================ softmax + epilogue ================================
+    reg_alloc<kFaRegsSoftmax>();
     const int t = (warp - 4) >> 2;          // query tile of this warpgroup
     const int quad = warp & 3;              // TMEM lane quadrant
     const int r = quad * 32 + lane;         // row of the tile
@@ -278,11 +292,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i > cmax) sv[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // row maximum: four independent chains of three-input max
+      float mxc[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 4; ++c) {
+        float a = max3(__uint_as_float(sv[c][0]), __uint_as_float(sv[c][1]), __uint_as_float(sv[c][2]));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+        for (int i = 3; i + 1 < 32; i += 2)
+          a = max3(a, __uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1]));
+        mxc[c] = fmaxf(a, __uint_as_float(sv[c][31]));
+      }
+      const float mx = fmaxf(fmaxf(mxc[0], mxc[1]), fmaxf(mxc[2], mxc[3]));
 
       // lazy rescale: raise m only when the tile maximum is far above it (warp-uniform,
       // because the O update below is a warp-collective TMEM access)
@@ -313,22 +333,35 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
 
       const float neg_m = -m * sl2;
-      float sum = 0.f;
+      // probabilities; four independent partial sums.  (kExp2OnFmaPipe moves every fourth
+      // exp2 from the MUFU to the FMA pipe.)
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[half * 2 + c][i]), sl2, neg_m));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[half * 2 + c][i + 1]), sl2, neg_m));
-            sum += p0 + p1;
+          for (int i = 0; i < 32; i += 4) {
+            const float x0 = fmaf(__uint_as_float(sv[half * 2 + c][i + 0]), sl2, neg_m);
+            const float x1 = fmaf(__uint_as_float(sv[half * 2 + c][i + 1]), sl2, neg_m);
+            const float x2 = fmaf(__uint_as_float(sv[half * 2 + c][i + 2]), sl2, neg_m);
+            const float x3 = fmaf(__uint_as_float(sv[half * 2 + c][i + 3]), sl2, neg_m);
+            const float p0 = fast_exp2(x0);
+            const float p1 = fast_exp2(x1);
+            const float p2 = fast_exp2(x2);
+            const float p3 = kExp2OnFmaPipe ? exp2_fma(x3) : fast_exp2(x3);
+            sum4[0] += p0;
+            sum4[1] += p1;
+            sum4[2] += p2;
+            sum4[3] += p3;
             pk[c * 16 + i / 2] = pack_bf16x2(p0, p1);
+            pk[c * 16 + i / 2 + 1] = pack_bf16x2(p2, p3);
           }
         }
         tmem_st_32x32b_x32(s_tmem + half * 32, pk);
       }
+      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       l += sum;
       tmem_st_wait();
       tc_fence_before_sync();

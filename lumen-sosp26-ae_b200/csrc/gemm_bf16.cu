@@ -72,6 +72,8 @@ bool use_pair_tiles() {
 
 inline int ceil_div_h(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
+constexpr int kSplitCounterSlots = 4096;  // output tiles a split-K launch may have
+
 // swapped dense path: tile geometry and split-K plan for M <= 128
 struct SwapPlan {
   int bn;       // activation rows per tile (UMMA N)
@@ -86,12 +88,15 @@ SwapPlan plan_swap(int M, int N, int K, int sms) {
   p.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   p.tiles = ceil_div_h(N, kBlockP) * ceil_div_h(M, p.bn);
   const int k_blocks = ceil_div_h(K, kBlockK);
+  // one unit per CTA: as many K slices as fit the SMs, at least 4 K blocks per slice
   int splits = sms / p.tiles;
-  const int max_splits = k_blocks / 4 > 0 ? k_blocks / 4 : 1;  // at least 4 K blocks per slice
+  const int max_splits = k_blocks / 4 > 0 ? k_blocks / 4 : 1;
   if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
+  if (splits < 1 || p.tiles > kSplitCounterSlots) splits = 1;
   p.splits = splits;
-  p.counter_bytes = (size_t(p.tiles) * sizeof(int) + 255) / 256 * 256;
+  // the counters own a fixed region at the head of the scratch buffer, so that partial
+  // sums of one shape never land where another shape keeps its counters
+  p.counter_bytes = size_t(kSplitCounterSlots) * sizeof(int);
   p.partial_bytes = splits > 1 ? size_t(p.tiles) * splits * p.bn * kBlockP * sizeof(float) : 0;
   return p;
 }

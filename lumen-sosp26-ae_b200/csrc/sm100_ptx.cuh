@@ -394,4 +394,38 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Register re-allocation between the warpgroups of a warp-specialised kernel: warpgroups
+// that only issue copies or MMAs give registers back, compute warpgroups take them.
+// Whole warpgroups must execute these (.sync.aligned); counts are multiples of 8.
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// three-input maximum (one instruction on sm_100)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA and integer pipes (no MUFU): split x into the nearest integer j and a
+// fraction f in [-0.5, 0.5], evaluate 2^f with a cubic (relative error below 7e-4, well
+// under the bf16 rounding the result receives) and add j to the exponent field.
+// Inputs below -127 give (denormal) zero.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -127.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: the sum's low mantissa bits hold j
+  const float j = t - 12582912.0f;
+  const float f = x - j;
+  float p = fmaf(f, 0.0555041087f, 0.240226507f);
+  p = fmaf(p, f, 0.693147181f);
+  p = fmaf(p, f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 }  // namespace b200

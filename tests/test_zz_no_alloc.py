@@ -64,8 +64,8 @@ def test_static_scratch_gemm_refuses_what_it_cannot_hold(cuda_pkg):
     rc = lib.lumen_b200_gemm_bf16_nt_static(a.data_ptr(), b.data_ptr(), c.data_ptr(), 256, 1024, 4096,
                                              4096, 4096, 1024, stream)
     assert rc == cuda_pkg._cabi.EUNSUPPORTED
-    # a plan larger than the array: M = 128, few tiles, many slices of a long K
-    m, n, k = 128, 896, 65536
+    # a plan larger than the array: M = 128 with a long K is cut into many slices
+    m, n, k = 128, 4096, 14336
     need = int(lib.lumen_b200_gemm_workspace_bytes(m, n, k))
     if need > int(lib.lumen_b200_gemm_static_scratch_limit()):
         a = torch.zeros((m, k), dtype=torch.bfloat16, device=DEV)
