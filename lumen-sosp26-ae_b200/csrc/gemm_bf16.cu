@@ -92,6 +92,9 @@ SwapPlan plan_swap(int M, int N, int K, int sms) {
   int splits = sms / p.tiles;
   const int max_splits = k_blocks / 4 > 0 ? k_blocks / 4 : 1;
   if (splits > max_splits) splits = max_splits;
+  // the last slice to arrive adds splits x BN partial rows on its own: bound that tail
+  const int max_by_tail = 512 / p.bn;  // 4 slices of 128 rows ... 16 slices of <= 32 rows
+  if (splits > max_by_tail) splits = max_by_tail;
   if (splits < 1 || p.tiles > kSplitCounterSlots) splits = 1;
   p.splits = splits;
   // the counters own a fixed region at the head of the scratch buffer, so that partial
@@ -106,10 +109,22 @@ SwapPlan plan_swap(int M, int N, int K, int sms) {
 
 using namespace b200;
 
+// The dense GEMM streams weights (swapped orientation, split-K) when there are few
+// activation rows, and also when the problem is so small that 256 x 256 tiles would
+// leave most CTA pairs idle (e.g. one GPU's column shard of a modest GEMM).
+static bool takes_streaming_path(int M, int N, int K, int sms) {
+  if (M <= 128) return true;
+  const long long pair_units =
+      static_cast<long long>((M + kPairTileM - 1) / kPairTileM) * ((N + kPairTileN - 1) / kPairTileN);
+  const long long swap_tiles = static_cast<long long>((N + kBlockP - 1) / kBlockP) * ((M + 127) / 128);
+  return pair_units * 5 < static_cast<long long>(sms / 2) * 2 && swap_tiles <= sms && K >= 512;
+}
+
 extern "C" size_t lumen_b200_gemm_workspace_bytes(int M, int N, int K) {
-  if (M <= 0 || N <= 0 || K <= 0 || M > 128) return 0;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int sms = device_sm_count();
   if (sms <= 0) return 0;
+  if (!takes_streaming_path(M, N, K, sms)) return 0;
   const SwapPlan p = plan_swap(M, N, K, sms);
   return p.splits > 1 ? p.counter_bytes + p.partial_bytes : 0;
 }
@@ -137,14 +152,15 @@ extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, in
   args.status = status;
 
   CUtensorMap mp, mq;
-  if (M > 128 && use_pair_tiles()) {
+  const bool streaming = takes_streaming_path(M, N, K, sms);
+  if (!streaming && use_pair_tiles()) {
     // CTA pairs: each CTA loads 128-row boxes of A and of B
     if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
     if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, kBlockP) != 0) return LUMEN_B200_ECUDA;
     const int units = ((M + kPairTileM - 1) / kPairTileM) * ((N + kPairTileN - 1) / kPairTileN);
     return launch_gemm_pair(mp, mq, args, units, st);
   }
-  if (M > 128) {
+  if (!streaming) {
     // P = A (128-row boxes), Q = B (256-row boxes)
     if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
     if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, 256) != 0) return LUMEN_B200_ECUDA;
@@ -216,7 +232,7 @@ extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights
   const uint64_t w_total_rows = uint64_t(E) * w_rows;
   CUtensorMap mp, mq;
   const int grid = sms;
-  if (rows_hint > 64) {
+  if (rows_hint > 128) {
     // tokens on the TMEM lanes, 128 rows per unit
     if (encode_tmap_bf16_2d(&mp, acts, max_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
     if (encode_tmap_bf16_2d(&mq, weights, w_total_rows, K, K, gated ? 128 : 256) != 0)
@@ -224,8 +240,12 @@ extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights
     return gated ? launch_gemm<256, 4, false, true, true>(mp, mq, args, grid, st)
                  : launch_gemm<256, 4, false, false, true>(mp, mq, args, grid, st);
   }
-  // few rows per expert: weights on the TMEM lanes
-  const int bn = rows_hint <= 16 ? 16 : rows_hint <= 32 ? 32 : 64;
+  // up to ~128 rows per expert: weights on the TMEM lanes, the expert's rows are the MMA's
+  // N dimension (sized per unit, so ragged expert loads waste little).  Beyond that the
+  // 128 x 256 token-major tile wins: a 128 x 128 MMA with both operands in shared memory is
+  // bound by shared-memory bandwidth (measured: 4.18 ms against 3.98 ms for the gated GEMM
+  // of the 256-expert configuration at 8192 tokens).
+  const int bn = rows_hint <= 16 ? 16 : rows_hint <= 32 ? 32 : rows_hint <= 64 ? 64 : (gated ? 128 : 256);
   if (encode_tmap_bf16_2d(&mp, weights, w_total_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
   if (encode_tmap_bf16_2d(&mq, acts, max_rows, K, K, bn) != 0) return LUMEN_B200_ECUDA;
   if (gated) {
@@ -234,8 +254,10 @@ extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights
         return launch_gemm<16, 6, true, true, true>(mp, mq, args, grid, st);
       case 32:
         return launch_gemm<32, 6, true, true, true>(mp, mq, args, grid, st);
-      default:
+      case 64:
         return launch_gemm<64, 5, true, true, true>(mp, mq, args, grid, st);
+      default:
+        return launch_gemm<128, 4, true, true, true>(mp, mq, args, grid, st);
     }
   }
   switch (bn) {
@@ -243,8 +265,10 @@ extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights
       return launch_gemm<16, 10, true, false, true>(mp, mq, args, grid, st);
     case 32:
       return launch_gemm<32, 10, true, false, true>(mp, mq, args, grid, st);
-    default:
+    case 64:
       return launch_gemm<64, 8, true, false, true>(mp, mq, args, grid, st);
+    default:
+      return launch_gemm<256, 4, true, false, true>(mp, mq, args, grid, st);
   }
 }
 

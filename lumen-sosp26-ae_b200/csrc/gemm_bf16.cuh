@@ -320,13 +320,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer ===================================
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBlockP, BN, 0, 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++it) {
         const Unit t = dec.decode(u);
+        // swapped orientation: the activation rows are the MMA's N, so a ragged unit
+        // only pays for its own rows (rounded up to the instruction granularity of 16)
+        const uint32_t idesc =
+            make_idesc_bf16(kBlockP, SWAP ? min(BN, (t.rows_valid + 15) & ~15) : BN, 0, 0);
         const int buf = it & 1;
         const uint32_t buf_phase = (it >> 1) & 1;
         if (!mbar_wait(smem_u32(&tail->tmem_empty[buf]), buf_phase ^ 1u, ctx, kWaitTmemEmpty)) {
@@ -434,8 +437,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float* ws_tile = nullptr;
         if (split_k)
           ws_tile = args.ws + (size_t(t.tile_id) * args.splits + t.split) * (size_t(BN) * kBlockP);
+        const int chunks_used = min(kChunks, (t.rows_valid + 31) / 32);  // columns the MMA wrote
 #pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
+        for (int c = 0; c < chunks_used; ++c) {
           float f[kChunkCols];
           if constexpr (kChunkCols == 32) {
             uint32_t v[32];
@@ -493,24 +497,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const bool last = tail->last_flag != 0;
           if (last) {
             __threadfence();
+            // [splits][BN rows][128 columns] fp32 -> out.  Thread = 4 consecutive columns
+            // of every fourth row; 16-byte loads, 8 rows x all slices in flight per pass.
             const float* base = args.ws + size_t(t.tile_id) * args.splits * (size_t(BN) * kBlockP);
-            constexpr int kRowsPerPass = 8;  // independent sums keep 8 x splits loads in flight
-            for (int r0 = 0; r0 < t.rows_valid; r0 += kRowsPerPass) {
-              float acc[kRowsPerPass];
+            const int c4 = (epi_tid & 31) * 4;
+            const int rgrp = epi_tid >> 5;  // 0..3
+            constexpr int kRowsPerPass = 8;
+            const bool vec_store = (args.ldo % 4 == 0) &&
+                                   ((reinterpret_cast<uintptr_t>(args.out) & 7) == 0);
+            for (int r0 = rgrp; r0 < t.rows_valid; r0 += 4 * kRowsPerPass) {
+              float4 acc[kRowsPerPass];
 #pragma unroll
-              for (int i = 0; i < kRowsPerPass; ++i) acc[i] = 0.f;
+              for (int i = 0; i < kRowsPerPass; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
               for (int s = 0; s < args.splits; ++s) {
-                const float* slice = base + size_t(s) * (size_t(BN) * kBlockP) + p;
+                const float* slice = base + size_t(s) * (size_t(BN) * kBlockP) + c4;
+                float4 v[kRowsPerPass];
 #pragma unroll
-                for (int i = 0; i < kRowsPerPass; ++i)
-                  if (r0 + i < BN) acc[i] += __ldcg(slice + (r0 + i) * kBlockP);
+                for (int i = 0; i < kRowsPerPass; ++i)  // all loads first: 8 in flight per thread
+                  v[i] = __ldcg(reinterpret_cast<const float4*>(slice + min(r0 + 4 * i, BN - 1) * kBlockP));
+#pragma unroll
+                for (int i = 0; i < kRowsPerPass; ++i) {
+                  acc[i].x += v[i].x;
+                  acc[i].y += v[i].y;
+                  acc[i].z += v[i].z;
+                  acc[i].w += v[i].w;
+                }
               }
-              if (col_ok) {
 #pragma unroll
-                for (int i = 0; i < kRowsPerPass; ++i)
-                  if (r0 + i < t.rows_valid)
-                    args.out[size_t(t.out_row + r0 + i) * args.ldo + t.out_col + p] =
-                        __float2bfloat16_rn(acc[i]);
+              for (int i = 0; i < kRowsPerPass; ++i) {
+                const int r = r0 + 4 * i;
+                if (r >= t.rows_valid) continue;
+                __nv_bfloat16* o = args.out + size_t(t.out_row + r) * args.ldo + t.out_col + c4;
+                if (vec_store && c4 + 4 <= t.cols_valid) {
+                  uint2 q;
+                  q.x = pack_bf16x2(acc[i].x, acc[i].y);
+                  q.y = pack_bf16x2(acc[i].z, acc[i].w);
+                  *reinterpret_cast<uint2*>(o) = q;
+                } else {
+                  if (c4 + 0 < t.cols_valid) o[0] = __float2bfloat16_rn(acc[i].x);
+                  if (c4 + 1 < t.cols_valid) o[1] = __float2bfloat16_rn(acc[i].y);
+                  if (c4 + 2 < t.cols_valid) o[2] = __float2bfloat16_rn(acc[i].z);
+                  if (c4 + 3 < t.cols_valid) o[3] = __float2bfloat16_rn(acc[i].w);
+                }
               }
             }
           }

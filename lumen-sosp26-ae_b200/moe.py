@@ -152,6 +152,21 @@ def permute_rows(x: torch.Tensor, routes: SortedRoutes, out: torch.Tensor | None
     return out
 
 
+_row_counts: dict = {}
+
+
+def _row_count(dev: torch.device, n: int) -> torch.Tensor:
+    """Device-resident int32 [n, 0] (the num_valid_ids form the row gather reads), cached."""
+    key = (dev.index, n)
+    t = _row_counts.get(key)
+    if t is None:
+        if len(_row_counts) > 4096:
+            _row_counts.clear()
+        t = torch.tensor([n, 0], dtype=torch.int32, device=dev)
+        _row_counts[key] = t
+    return t
+
+
 def gather_rows(rows: torch.Tensor, index: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """out[i,:] = rows[index[i],:] (an index >= len(rows) gives a zero row); bf16 rows, int32 index."""
     dev = _need_cuda(rows, index)
@@ -163,7 +178,7 @@ def gather_rows(rows: torch.Tensor, index: torch.Tensor, out: torch.Tensor | Non
         out = torch.empty((n, H), dtype=torch.bfloat16, device=dev)
     if n == 0:
         return out
-    count = torch.tensor([n, R], dtype=torch.int32, device=dev)
+    count = _row_count(dev, n)
     with _cabi.on_device(dev):
         rc = _cabi.load().lumen_b200_moe_permute_rows(
             rows.data_ptr(), index.data_ptr(), count.data_ptr(), out.data_ptr(), R, H, n, _stream(dev))

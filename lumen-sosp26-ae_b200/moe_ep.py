@@ -62,17 +62,13 @@ def regroup_plan(recv_counts: np.ndarray) -> RegroupPlan:
     seg_arrival_start = np.concatenate([[0], np.cumsum(rc.reshape(-1))])[:-1].reshape(world, e_local)
     expert_counts = rc.sum(axis=0)
     expert_offsets = np.concatenate([[0], np.cumsum(expert_counts)])
-    # grouped order: (e, src) segments; within an expert the sources keep rank order
-    before_src = np.cumsum(rc, axis=0) - rc  # rows of expert e from sources < src
-    seg_grouped_start = expert_offsets[:-1][None, :] + before_src
-    gather = np.empty(total, dtype=np.int32)
-    for src in range(world):
-        for e in range(e_local):
-            n = int(rc[src, e])
-            if n:
-                g0 = int(seg_grouped_start[src, e])
-                gather[g0:g0 + n] = np.arange(int(seg_arrival_start[src, e]),
-                                              int(seg_arrival_start[src, e]) + n, dtype=np.int32)
+    # grouped order: (e, src) segments; within an expert the sources keep rank order.
+    # Position g of the grouped buffer lies in segment k: it reads arrival row
+    # seg_arrival_start[k] + (g - seg_grouped_start[k]).
+    seg_len = rc.T.reshape(-1)                                   # (e, src) order
+    seg_grouped_start = np.concatenate([[0], np.cumsum(seg_len)])[:-1]
+    shift = seg_arrival_start.T.reshape(-1) - seg_grouped_start
+    gather = (np.repeat(shift, seg_len) + np.arange(total, dtype=np.int64)).astype(np.int32)
     scatter = np.empty(total, dtype=np.int32)
     scatter[gather] = np.arange(total, dtype=np.int32)
     return RegroupPlan(gather=gather, scatter=scatter,
@@ -131,10 +127,14 @@ class ExpertParallelMoE:
 
         # 3) regroup by expert, run the experts, restore arrival order
         if R > 0:
-            grouped = ops.gather(recv, ops.from_host(plan.gather, torch.int32))
-            y = ops.expert_ffn(grouped, ops.from_host(plan.expert_offsets, torch.int32),
-                               ops.from_host(plan.expert_counts, torch.int32), w13_local, w2_local)
-            y_back = ops.gather(y, ops.from_host(plan.scatter, torch.int32))
+            # one upload: [gather | scatter | expert_offsets | expert_counts]
+            packed = ops.from_host(np.concatenate([plan.gather, plan.scatter, plan.expert_offsets,
+                                                   plan.expert_counts]), torch.int32)
+            gather_d, scatter_d = packed[:R], packed[R:2 * R]
+            offsets_d, counts_d = packed[2 * R:2 * R + El + 1], packed[2 * R + El + 1:]
+            grouped = ops.gather(recv, gather_d)
+            y = ops.expert_ffn(grouped, offsets_d, counts_d, w13_local, w2_local)
+            y_back = ops.gather(y, scatter_d)
         else:
             y_back = recv
 
@@ -188,7 +188,8 @@ class CudaOps:
         return t.cpu().numpy()
 
     def from_host(self, a, dtype):
-        return torch.from_numpy(np.ascontiguousarray(a)).to(device=self.dev, dtype=dtype)
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(dtype)
+        return t.pin_memory().to(self.dev, non_blocking=True)
 
     def empty(self, shape, dtype):
         return torch.empty(shape, dtype=dtype, device=self.dev)

@@ -129,6 +129,7 @@ def test_forward_golden(cuda_pkg, case, k, router):
     (1, 512, 256, 16, 4, False),        # one token
     (64, 1024, 512, 32, 8, False),      # a few rows per expert: weight-streaming orientation
     (200, 512, 384, 8, 2, True),        # ~50 rows per expert
+    (400, 512, 256, 8, 2, True),        # 100 rows per expert: weight-major, MMA N sized per unit
     (1024, 512, 256, 8, 2, True),       # 256 rows per expert: token-major orientation
     (700, 384, 640, 4, 2, True),        # ragged tiles in every dimension
 ])
