@@ -197,10 +197,10 @@ def run_b200_arm(args) -> None:
     dev = torch.device("cuda", local_rank)
     dist = None
     if world > 1:
-        # NCCL prints its version banner on stdout when NCCL_DEBUG=VERSION; stdout carries
-        # the one JSON line only
-        if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL prints its version banner on stdout when NCCL_DEBUG is VERSION or WARN;
+        # stdout carries the one JSON line only
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
+            del os.environ["NCCL_DEBUG"]
         import torch.distributed as dist_mod
 
         dist = dist_mod
@@ -500,6 +500,8 @@ def run_ep_case(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
+        del os.environ["NCCL_DEBUG"]  # its version banner goes to stdout, which carries the JSON line
     dist.init_process_group("nccl", device_id=dev)
     if rank == 0:
         entry.build()
@@ -526,8 +528,11 @@ def run_ep_case(args) -> None:
     for e in range(El):
         w13[e] = randn_bf16((2 * I, H), 0.02)
         w2[e] = randn_bf16((H, I), 0.02)
-    ops = pkg.moe_ep.CudaOps(dev, tokens_global=T, experts=E, topk=K)
-    ep = pkg.moe_ep.ExpertParallelMoE(experts=E, topk=K, ops=ops)
+    if args.transport == "peer":
+        ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=Tl, hidden=H, inter=I, experts=E, topk=K, device=dev)
+    else:
+        ops = pkg.moe_ep.CudaOps(dev, tokens_global=T, experts=E, topk=K)
+        ep = pkg.moe_ep.ExpertParallelMoE(experts=E, topk=K, ops=ops)
     for _ in range(max(args.warmup, 2)):
         ep.forward(x, w13, w2, logits=logits)
     dist.barrier()
@@ -542,13 +547,22 @@ def run_ep_case(args) -> None:
     t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    # phase breakdown of one more forward on rank 0 (events between the phases)
+    marks: list = []
+    ep.forward(x, w13, w2, logits=logits, marks=marks)
+    torch.cuda.synchronize()
+    phases = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])}
     status = pkg.device_status()
     if rank == 0:
         fl = 6.0 * T * K * H * I
         print(json.dumps({"case": args.case, "n_gpus": world, "ms": ms, "tokens_per_s": T / ms * 1e3,
+                          "phase_ms_rank0": phases,
                           "tflops": fl / ms / 1e9, "tokens": T, "experts": E, "topk": K,
-                          "parallelism": f"expert-parallel x{world}, tokens {Tl}/rank, experts {El}/rank, NCCL all_to_all",
-                          "timing": "eager (one host read of the per-expert counts per forward)",
+                          "parallelism": f"expert-parallel x{world}, tokens {Tl}/rank, experts {El}/rank",
+                          "transport": ("dispatch/return kernels storing into peer memory over NVLink, no host read"
+                                        if args.transport == "peer" else
+                                        "NCCL all_to_all_single, one host read of the per-expert counts per forward"),
+                          "timing": "eager launches",
                           "status": status}), flush=True)
     dist.destroy_process_group()
 
@@ -565,6 +579,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--transport", choices=("peer", "nccl"), default="peer",
+                    help="--case ep:*: how rows cross GPUs")
     ap.add_argument("--eager", action="store_true", help="--case: time eager launches instead of graph replays")
     ap.add_argument("--case", default=None, help="run one operator case instead of the sweep (see run_case)")
     args = ap.parse_args()

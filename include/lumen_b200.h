@@ -174,6 +174,40 @@ int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights, void* out
 int lumen_b200_moe_combine(const void* y, const void* route_pos, const void* topk_weights,
                            void* out, int T, int H, int k, void* stream);
 
+/* ---------------------------------------------- MoE, expert parallel (G GPUs) -- */
+/* Tokens and experts are sharded over G GPUs (expert e on GPU e / (E/G)); each GPU sorts
+ * its own routes compactly (route_group = 1).  `counts` is the G x E matrix of every
+ * GPU's expert_counts (all-gathered by the caller).  The reference has no multi-GPU
+ * path; these stand where its single-GPU gather (_input_fetch_async,
+ * datasets/inference/moe/lumen/fused_moe.py:246-271) and write-back
+ * (_stage2_write_back, :864-888) stand, across GPUs. */
+
+/* From `counts` [G,E] int32 derive, for GPU `rank`:
+ *   send_dst_start[E]     row in the owner's grouped buffer where this GPU's rows of expert e start
+ *   local_offsets[E/G+1], local_counts[E/G]   grouped layout of this GPU's experts
+ *   seg_start[E/G*G+1]    first grouped row of the rows GPU s sent for local expert le (index le*G+s)
+ *   seg_home_row[E/G*G]   row of GPU s's compact sorted order those rows came from */
+int lumen_b200_moe_ep_plan(const void* counts, int G, int E, int rank, void* send_dst_start,
+                           void* local_offsets, void* local_counts, void* seg_start,
+                           void* seg_home_row, void* stream);
+
+/* Dispatch: copy x[token] of every compactly sorted route of this GPU straight into the
+ * owner GPU's grouped buffer.  peer_buffers (host array of G device pointers, each
+ * [capacity_rows, H] bf16, 16-byte aligned, peer-accessible; entry `rank` is this GPU's
+ * own buffer).  row_expert[pos] = expert of sorted position pos (the sorted_expert_ids of
+ * a route_group = 1 sort).  Rows that would fall outside capacity_rows are dropped and
+ * flagged in the device status word.  Callers synchronise the GPUs before reading. */
+int lumen_b200_moe_ep_dispatch(const void* x, const void* sorted_token_ids, const void* row_expert,
+                               const void* expert_offsets, const void* send_dst_start,
+                               const void* num_valid_ids, const void* const* peer_buffers, int G,
+                               int T, int H, int E, int max_rows, int capacity_rows, void* stream);
+
+/* Return: copy every grouped output row y[g] back to the GPU it came from, at its row in
+ * that GPU's compact sorted order (peer_buffers: G pointers to [home_capacity_rows, H]). */
+int lumen_b200_moe_ep_return(const void* y, const void* seg_start, const void* seg_home_row,
+                             const void* const* peer_buffers, int G, int El, int H, int max_rows,
+                             int home_capacity_rows, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

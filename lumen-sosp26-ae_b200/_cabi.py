@@ -65,6 +65,18 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
          c_void_p],
     ),
+    "lumen_b200_moe_ep_plan": (
+        c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "lumen_b200_moe_ep_dispatch": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.POINTER(c_void_p), c_int,
+         c_int, c_int, c_int, c_int, c_int, c_void_p],
+    ),
+    "lumen_b200_moe_ep_return": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_int, c_int,
+         c_void_p],
+    ),
     "lumen_b200_moe_combine": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
 }

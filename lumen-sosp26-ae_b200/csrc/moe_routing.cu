@@ -469,3 +469,219 @@ extern "C" int lumen_b200_moe_combine(const void* y, const void* route_pos, cons
                                            static_cast<__nv_bfloat16*>(out), T, H, k);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
+
+// ===========================================================================
+// Expert-parallel dispatch and return over peer memory (NVLink / NVSwitch).
+//
+// Tokens are sharded over the G GPUs, experts too (expert e lives on GPU e / El).  Instead
+// of packing a send buffer and calling a collective, the row gather of the dispatch
+// writes each row straight into its final place in the owning GPU's expert-grouped
+// buffer with peer stores, and after the expert GEMMs the owner writes every output row
+// straight back into the source GPU's buffer.  Every GPU derives all offsets from the
+// same G x E count matrix, so no sizes travel and the host reads nothing.
+// ===========================================================================
+namespace b200 {
+
+constexpr int kMaxEpRanks = 16;
+
+struct PeerPtrs {
+  void* p[kMaxEpRanks];
+};
+
+// One CTA.  counts[s][e] = routes of GPU s for global expert e.
+//   send_dst_start[e]          row in the owner's grouped buffer where this GPU's rows of expert e start
+//   local_offsets[le], local_counts[le]   grouped layout of this GPU's own experts (El + 1 / El entries)
+//   seg_start[le * G + s]      first grouped row of the rows that GPU s sent for local expert le (El*G + 1)
+//   seg_home_row[le * G + s]   row in GPU s's compact sorted order where those rows came from
+__global__ void __launch_bounds__(1024)
+    moe_ep_plan_kernel(const int* __restrict__ counts, int G, int E, int rank, int* __restrict__ send_dst_start,
+                       int* __restrict__ local_offsets, int* __restrict__ local_counts,
+                       int* __restrict__ seg_start, int* __restrict__ seg_home_row) {
+  __shared__ int s_prefix[kMaxExperts + 1];  // exclusive prefix over experts of the column totals
+  __shared__ int s_warp[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int El = E / G;
+
+  // block-wide exclusive scan over e of value(e); result in s_prefix[0..E]
+  auto block_scan = [&](int v) {
+    int incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_warp[lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= d) w += o;
+      }
+      s_warp[lane] = w;
+    }
+    __syncthreads();
+    const int base = warp == 0 ? 0 : s_warp[warp - 1];
+    if (tid < E) s_prefix[tid] = base + incl - v;
+    if (tid == E - 1) s_prefix[E] = base + incl;
+    __syncthreads();
+  };
+
+  const int e = tid;
+  int total = 0, before_me = 0;
+  if (e < E) {
+    for (int s = 0; s < G; ++s) {
+      const int c = counts[s * E + e];
+      if (s < rank) before_me += c;
+      total += c;
+    }
+  }
+  block_scan(e < E ? total : 0);
+  if (e < E) {
+    const int owner = e / El;
+    send_dst_start[e] = s_prefix[e] - s_prefix[owner * El] + before_me;
+    if (owner == rank) {
+      const int le = e - rank * El;
+      const int off = s_prefix[e] - s_prefix[rank * El];
+      local_offsets[le] = off;
+      local_counts[le] = total;
+      int run = off;
+      for (int s = 0; s < G; ++s) {
+        seg_start[le * G + s] = run;
+        run += counts[s * E + e];
+      }
+      if (le == El - 1) {
+        local_offsets[El] = run;
+        seg_start[El * G] = run;
+      }
+    }
+  }
+  __syncthreads();
+  // home rows: exclusive prefix over ALL experts of each source GPU's own counts
+  for (int s = 0; s < G; ++s) {
+    block_scan(e < E ? counts[s * E + e] : 0);
+    if (e < E && e / El == rank) seg_home_row[(e - rank * El) * G + s] = s_prefix[e];
+    __syncthreads();
+  }
+}
+
+// Dispatch: for every compactly sorted route of this GPU, copy the token's row into the
+// owner GPU's grouped buffer.  One CTA per route (grid-stride), 16-byte copies.
+__global__ void __launch_bounds__(256)
+    moe_ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ sorted_token_ids,
+                           const int* __restrict__ row_expert, const int* __restrict__ expert_offsets,
+                           const int* __restrict__ send_dst_start, const int* __restrict__ num_valid_ids,
+                           PeerPtrs peers, int T, int H, int El, int capacity_rows, int* status) {
+  const int total = num_valid_ids[0];
+  const int chunks = H / 8;
+  for (int pos = blockIdx.x; pos < total; pos += gridDim.x) {
+    const int token = sorted_token_ids[pos] & 0xffffff;
+    const int e = row_expert[pos];
+    if (token >= T || e < 0) continue;
+    const int dst_row = send_dst_start[e] + (pos - expert_offsets[e]);
+    if (dst_row < 0 || dst_row >= capacity_rows) {  // never write outside the peer's buffer
+      if (threadIdx.x == 0) atomicCAS(status, 0, (32 << 16) | (blockIdx.x & 0xffff));
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peers.p[e / El]) + size_t(dst_row) * H);
+    const uint4* src = reinterpret_cast<const uint4*>(x + size_t(token) * H);
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+  }
+  __threadfence_system();
+}
+
+// Return: every grouped output row goes back to the GPU it came from, at the row of that
+// GPU's compact sorted order, ready for its weighted combine.
+__global__ void __launch_bounds__(256)
+    moe_ep_return_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ seg_start,
+                         const int* __restrict__ seg_home_row, PeerPtrs peers, int H, int G, int nseg,
+                         int home_capacity_rows, int* status) {
+  const int total = seg_start[nseg];
+  const int chunks = H / 8;
+  for (int g = blockIdx.x; g < total; g += gridDim.x) {
+    // segment k with seg_start[k] <= g < seg_start[k + 1] (empty segments are skipped)
+    int lo = 0, hi = nseg;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (seg_start[mid] <= g) lo = mid; else hi = mid;
+    }
+    const int k = lo;
+    const int src_gpu = k % G;
+    const int dst_row = seg_home_row[k] + (g - seg_start[k]);
+    if (dst_row < 0 || dst_row >= home_capacity_rows) {
+      if (threadIdx.x == 0) atomicCAS(status, 0, (33 << 16) | (blockIdx.x & 0xffff));
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peers.p[src_gpu]) + size_t(dst_row) * H);
+    const uint4* src = reinterpret_cast<const uint4*>(y + size_t(g) * H);
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+  }
+  __threadfence_system();
+}
+
+}  // namespace b200
+
+extern "C" int lumen_b200_moe_ep_plan(const void* counts, int G, int E, int rank, void* send_dst_start,
+                                       void* local_offsets, void* local_counts, void* seg_start,
+                                       void* seg_home_row, void* stream) {
+  if (!counts || !send_dst_start || !local_offsets || !local_counts || !seg_start || !seg_home_row)
+    return LUMEN_B200_EINVAL;
+  if (G <= 0 || G > kMaxEpRanks || E <= 0 || E > kMaxExperts || E % G != 0 || rank < 0 || rank >= G)
+    return LUMEN_B200_EINVAL;
+  moe_ep_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const int*>(counts), G, E, rank, static_cast<int*>(send_dst_start),
+      static_cast<int*>(local_offsets), static_cast<int*>(local_counts), static_cast<int*>(seg_start),
+      static_cast<int*>(seg_home_row));
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_ep_dispatch(const void* x, const void* sorted_token_ids, const void* row_expert,
+                                           const void* expert_offsets, const void* send_dst_start,
+                                           const void* num_valid_ids, const void* const* peer_buffers,
+                                           int G, int T, int H, int E, int max_rows, int capacity_rows,
+                                           void* stream) {
+  if (!x || !sorted_token_ids || !row_expert || !expert_offsets || !send_dst_start || !num_valid_ids ||
+      !peer_buffers)
+    return LUMEN_B200_EINVAL;
+  if (G <= 0 || G > kMaxEpRanks || E % G != 0 || T <= 0 || H <= 0 || H % 8 != 0 || max_rows <= 0 ||
+      capacity_rows <= 0)
+    return LUMEN_B200_EINVAL;
+  PeerPtrs peers{};
+  for (int g = 0; g < G; ++g) {
+    if (!peer_buffers[g] || (reinterpret_cast<uintptr_t>(peer_buffers[g]) & 15)) return LUMEN_B200_EINVAL;
+    peers.p[g] = const_cast<void*>(peer_buffers[g]);
+  }
+  int* status = device_status_word();
+  const int sms = device_sm_count();
+  if (!status || sms <= 0) return LUMEN_B200_ECUDA;
+  const int grid = max_rows < sms * 16 ? max_rows : sms * 16;
+  moe_ep_dispatch_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const int*>(sorted_token_ids),
+      static_cast<const int*>(row_expert), static_cast<const int*>(expert_offsets),
+      static_cast<const int*>(send_dst_start), static_cast<const int*>(num_valid_ids), peers, T, H, E / G,
+      capacity_rows, status);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_ep_return(const void* y, const void* seg_start, const void* seg_home_row,
+                                         const void* const* peer_buffers, int G, int El, int H, int max_rows,
+                                         int home_capacity_rows, void* stream) {
+  if (!y || !seg_start || !seg_home_row || !peer_buffers) return LUMEN_B200_EINVAL;
+  if (G <= 0 || G > kMaxEpRanks || El <= 0 || H <= 0 || H % 8 != 0 || max_rows <= 0 ||
+      home_capacity_rows <= 0)
+    return LUMEN_B200_EINVAL;
+  PeerPtrs peers{};
+  for (int g = 0; g < G; ++g) {
+    if (!peer_buffers[g] || (reinterpret_cast<uintptr_t>(peer_buffers[g]) & 15)) return LUMEN_B200_EINVAL;
+    peers.p[g] = const_cast<void*>(peer_buffers[g]);
+  }
+  int* status = device_status_word();
+  const int sms = device_sm_count();
+  if (!status || sms <= 0) return LUMEN_B200_ECUDA;
+  const int grid = max_rows < sms * 16 ? max_rows : sms * 16;
+  moe_ep_return_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y), static_cast<const int*>(seg_start),
+      static_cast<const int*>(seg_home_row), peers, H, G, El * G, home_capacity_rows, status);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}

@@ -77,6 +77,41 @@ def regroup_plan(recv_counts: np.ndarray) -> RegroupPlan:
                        recv_splits=recv_splits)
 
 
+@dataclass
+class PeerPlan:
+    """What lumen_b200_moe_ep_plan computes on the device, restated in numpy (used by the
+    tests and as the specification of the kernel)."""
+
+    send_dst_start: np.ndarray  # [E]
+    local_offsets: np.ndarray   # [El + 1]
+    local_counts: np.ndarray    # [El]
+    seg_start: np.ndarray       # [El * G + 1], index le * G + s
+    seg_home_row: np.ndarray    # [El * G]
+
+
+def peer_plan(counts: np.ndarray, rank: int) -> PeerPlan:
+    """counts[s, e] = routes of GPU s for global expert e."""
+    c = np.asarray(counts, dtype=np.int64)
+    G, E = c.shape
+    El = experts_per_rank(E, G)
+    total = c.sum(axis=0)
+    prefix = np.concatenate([[0], np.cumsum(total)])
+    owner_base = prefix[(np.arange(E) // El) * El]
+    before_me = c[:rank].sum(axis=0)
+    send_dst_start = prefix[:-1] - owner_base + before_me
+    mine = slice(rank * El, (rank + 1) * El)
+    local_counts = total[mine]
+    local_offsets = np.concatenate([[0], np.cumsum(local_counts)])
+    before_src = np.cumsum(c[:, mine], axis=0) - c[:, mine]          # [G, El]
+    seg_start = (local_offsets[:-1][:, None] + before_src.T).reshape(-1)  # (le, s) order
+    seg_start = np.concatenate([seg_start, [local_offsets[-1]]])
+    home = np.cumsum(c, axis=1) - c                                     # [G, E] exclusive over experts
+    seg_home_row = home[:, mine].T.reshape(-1)
+    i32 = np.int32
+    return PeerPlan(send_dst_start.astype(i32), local_offsets.astype(i32), local_counts.astype(i32),
+                    seg_start.astype(i32), seg_home_row.astype(i32))
+
+
 class ExpertParallelMoE:
     """One rank's side of the expert-parallel forward.
 
@@ -102,12 +137,23 @@ class ExpertParallelMoE:
         self.last_plan: RegroupPlan | None = None
         self.last_send_splits: np.ndarray | None = None
 
-    def forward(self, x, w13_local, w2_local, *, logits=None, w_router=None):
+    def forward(self, x, w13_local, w2_local, *, logits=None, w_router=None, marks=None):
+        """`marks`, if a list, receives (label, CUDA event) pairs recorded on the current
+        stream after each phase (measurement aid; events need a CUDA device)."""
         ops, G, El = self.ops, self.world, self.e_local
         T, H = x.shape
+
+        def mark(label):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((label, ev))
+
+        mark("start")
         ids, wts = ops.route(x, logits=logits, w_router=w_router)
         routes = ops.sort(ids, wts, self.E)
         rows = ops.permute(x, routes)  # [T*k, H], grouped by destination rank already
+        mark("route+sort+permute")
 
         # 1) exchange per-expert counts: I send counts[g*El:(g+1)*El] to rank g
         counts = routes.expert_counts
@@ -119,11 +165,13 @@ class ExpertParallelMoE:
         in_splits = send_splits(counts_h, G)
         self.last_plan, self.last_send_splits = plan, in_splits
         R = int(plan.recv_splits.sum())
+        mark("counts exchange + host plan")
 
         # 2) dispatch the rows
         recv = ops.empty((R, H), rows.dtype)
         dist.all_to_all_single(recv, rows[: int(in_splits.sum())], plan.recv_splits.tolist(),
                                in_splits.tolist(), group=self.group)
+        mark("dispatch all_to_all")
 
         # 3) regroup by expert, run the experts, restore arrival order
         if R > 0:
@@ -133,8 +181,11 @@ class ExpertParallelMoE:
             gather_d, scatter_d = packed[:R], packed[R:2 * R]
             offsets_d, counts_d = packed[2 * R:2 * R + El + 1], packed[2 * R + El + 1:]
             grouped = ops.gather(recv, gather_d)
+            mark("regroup gather")
             y = ops.expert_ffn(grouped, offsets_d, counts_d, w13_local, w2_local)
+            mark("expert GEMMs")
             y_back = ops.gather(y, scatter_d)
+            mark("restore gather")
         else:
             y_back = recv
 
@@ -143,8 +194,12 @@ class ExpertParallelMoE:
         dist.all_to_all_single(ret, y_back, in_splits.tolist(), plan.recv_splits.tolist(),
                                group=self.group)
 
+        mark("return all_to_all")
+
         # 5) weighted combine over each token's k routes
-        return ops.combine(ret, routes, wts, T)
+        out = ops.combine(ret, routes, wts, T)
+        mark("combine")
+        return out
 
 
 class CudaOps:
@@ -193,3 +248,117 @@ class CudaOps:
 
     def empty(self, shape, dtype):
         return torch.empty(shape, dtype=dtype, device=self.dev)
+
+
+class PeerExpertParallelMoE:
+    """Expert-parallel forward whose dispatch and return are this library's own kernels
+    writing over NVLink into the peers' buffers (symmetric memory), instead of a packed send
+    buffer plus all_to_all.  The host reads nothing during a forward: every GPU derives the
+    same offsets from the all-gathered G x E count matrix on the device.
+
+      route -> compact sort -> all_gather(counts) -> plan -> dispatch (peer stores)
+      -> barrier -> grouped GEMMs on the received rows -> return (peer stores)
+      -> barrier -> weighted combine
+
+    Buffers are sized for the worst case (every route of every GPU lands on one GPU).
+    Construction is collective (symmetric-memory rendezvous)."""
+
+    def __init__(self, *, tokens_local: int, hidden: int, inter: int, experts: int, topk: int,
+                 device: torch.device, group=None):
+        import ctypes
+        import os
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _cabi, moe
+
+        # plain peer loads/stores only: no NVLink multicast binding of these buffers
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        self.moe, self._cabi = moe, _cabi
+        self.group = group if group is not None else dist.group.WORLD
+        self.G = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.T, self.H, self.I, self.E, self.k = tokens_local, hidden, inter, experts, topk
+        self.El = experts_per_rank(experts, self.G)
+        self.dev = device
+        self.capacity = tokens_local * self.G * topk
+        self.home_rows = moe.max_padded_routes(tokens_local, topk, experts, 1)
+        bf16, i32 = torch.bfloat16, torch.int32
+        self.recv = symm_mem.empty((self.capacity, hidden), dtype=bf16, device=device)
+        self.ret = symm_mem.empty((self.home_rows, hidden), dtype=bf16, device=device)
+        self._recv_hdl = symm_mem.rendezvous(self.recv, self.group)
+        self._ret_hdl = symm_mem.rendezvous(self.ret, self.group)
+        ptr_array = ctypes.c_void_p * self.G
+        self._recv_peers = ptr_array(*[int(p) for p in self._recv_hdl.buffer_ptrs])
+        self._ret_peers = ptr_array(*[int(p) for p in self._ret_hdl.buffer_ptrs])
+        self.routes = moe.alloc_sorted_routes(tokens_local, topk, experts, device, group=1)
+        need = int(_cabi.load().lumen_b200_moe_sort_scratch_bytes(tokens_local, experts, topk))
+        self.scratch = torch.empty((max(need, 4),), dtype=torch.uint8, device=device)
+        self.topk_ids = torch.empty((tokens_local, topk), dtype=i32, device=device)
+        self.topk_weights = torch.empty((tokens_local, topk), dtype=torch.float32, device=device)
+        self.logits = torch.empty((tokens_local, experts), dtype=torch.float32, device=device)
+        self.count_matrix = torch.zeros((self.G, experts), dtype=i32, device=device)
+        self.send_dst_start = torch.zeros((experts,), dtype=i32, device=device)
+        self.local_offsets = torch.zeros((self.El + 1,), dtype=i32, device=device)
+        self.local_counts = torch.zeros((self.El,), dtype=i32, device=device)
+        self.seg_start = torch.zeros((self.El * self.G + 1,), dtype=i32, device=device)
+        self.seg_home_row = torch.zeros((self.El * self.G,), dtype=i32, device=device)
+        self.h = torch.empty((self.capacity, inter), dtype=bf16, device=device)
+        self.y = torch.empty((self.capacity, hidden), dtype=bf16, device=device)
+        self.out = torch.empty((tokens_local, hidden), dtype=bf16, device=device)
+        self._flag = torch.zeros((1,), dtype=torch.float32, device=device)
+        self.rows_hint = max(1, (tokens_local * self.G * topk + experts - 1) // experts)
+
+        class _Local:
+            pass
+
+        self._local = _Local()
+        self._local.expert_offsets, self._local.expert_counts = self.local_offsets, self.local_counts
+
+    def _gpu_barrier(self):
+        # stream-ordered rendezvous of all GPUs: nobody passes before everybody's earlier
+        # kernels (the peer stores) have completed
+        dist.all_reduce(self._flag, group=self.group)
+
+    def forward(self, x, w13_local, w2_local, *, logits=None, w_router=None, marks=None):
+        moe, lib = self.moe, self._cabi.load()
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+
+        def mark(label):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((label, ev))
+
+        mark("start")
+        if logits is None:
+            logits = moe.router_logits(x, w_router, out=self.logits)
+        moe.route_topk(logits, self.k, ids_out=self.topk_ids, weights_out=self.topk_weights)
+        r = moe.build_sorted_routes(topk_ids=self.topk_ids, topk_weights=self.topk_weights,
+                                    experts=self.E, out=self.routes, scratch=self.scratch, group=1)
+        mark("route+sort")
+        dist.all_gather_into_tensor(self.count_matrix.view(-1), r.expert_counts, group=self.group)
+        with self._cabi.on_device(self.dev):
+            self._cabi.check("lumen_b200_moe_ep_plan", lib.lumen_b200_moe_ep_plan(
+                self.count_matrix.data_ptr(), self.G, self.E, self.rank, self.send_dst_start.data_ptr(),
+                self.local_offsets.data_ptr(), self.local_counts.data_ptr(), self.seg_start.data_ptr(),
+                self.seg_home_row.data_ptr(), stream))
+            mark("counts all_gather + plan")
+            self._cabi.check("lumen_b200_moe_ep_dispatch", lib.lumen_b200_moe_ep_dispatch(
+                x.data_ptr(), r.sorted_token_ids.data_ptr(), r.sorted_expert_ids.data_ptr(),
+                r.expert_offsets.data_ptr(), self.send_dst_start.data_ptr(), r.num_valid_ids.data_ptr(),
+                self._recv_peers, self.G, self.T, self.H, self.E, self.T * self.k, self.capacity, stream))
+        self._gpu_barrier()
+        mark("dispatch (peer stores) + barrier")
+        moe.grouped_gemm(self.recv, w13_local, self._local, gated=True, rows_hint=self.rows_hint, out=self.h)
+        moe.grouped_gemm(self.h, w2_local, self._local, gated=False, rows_hint=self.rows_hint, out=self.y)
+        mark("expert GEMMs")
+        with self._cabi.on_device(self.dev):
+            self._cabi.check("lumen_b200_moe_ep_return", lib.lumen_b200_moe_ep_return(
+                self.y.data_ptr(), self.seg_start.data_ptr(), self.seg_home_row.data_ptr(),
+                self._ret_peers, self.G, self.El, self.H, self.capacity, self.home_rows, stream))
+        self._gpu_barrier()
+        mark("return (peer stores) + barrier")
+        out = moe.combine(self.ret, r, self.topk_weights, self.T, out=self.out)
+        mark("combine")
+        return out

@@ -79,6 +79,36 @@ def _worker(rank, world, port, result_dir):
             ids, w = moe_oracle.route_topk(logits, kk)
             want = moe_oracle.moe_reference(d["x"], d["w13"], d["w2"], ids, w)[t0:t1]
             torch.testing.assert_close(out.cpu().float(), want.float(), rtol=2e-2, atol=2e-2)
+        # ---- MoE: the same forward with this library's peer-memory dispatch and return
+        import numpy as np
+
+        for (T, H, I, E, kk, skew) in ((64, 512, 256, 16, 4, False), (256, 512, 384, 8, 2, True)):
+            d = moe_oracle.moe_inputs(T, H, I, E, 20260319 + T, with_router=False)
+            logits = d["logits"].clone()
+            if skew:
+                logits[:, E - E // world:] += 3.0
+                logits[:, 0] = -50.0
+            tl, el = T // world, E // world
+            t0, t1 = rank * tl, (rank + 1) * tl
+            ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=tl, hidden=H, inter=I, experts=E, topk=kk, device=dev)
+            w13, w2 = d["w13"][rank * el:(rank + 1) * el].to(dev), d["w2"][rank * el:(rank + 1) * el].to(dev)
+            ids, w = moe_oracle.route_topk(logits, kk)
+            want = moe_oracle.moe_reference(d["x"], d["w13"], d["w2"], ids, w)[t0:t1]
+            for _ in range(2):  # twice: the second forward reuses every buffer
+                out = ep.forward(d["x"][t0:t1].to(dev), w13, w2, logits=logits[t0:t1].to(dev))
+                torch.cuda.synchronize()
+                torch.testing.assert_close(out.cpu().float(), want.float(), rtol=2e-2, atol=2e-2)
+            # the device plan equals its numpy specification
+            counts = ep.count_matrix.cpu().numpy()
+            ref = pkg.moe_ep.peer_plan(counts, rank)
+            assert np.array_equal(ep.send_dst_start.cpu().numpy(), ref.send_dst_start)
+            assert np.array_equal(ep.local_offsets.cpu().numpy(), ref.local_offsets)
+            assert np.array_equal(ep.local_counts.cpu().numpy(), ref.local_counts)
+            assert np.array_equal(ep.seg_start.cpu().numpy(), ref.seg_start)
+            assert np.array_equal(ep.seg_home_row.cpu().numpy(), ref.seg_home_row)
+            want_counts = np.stack([np.bincount(ids[r * tl:(r + 1) * tl].numpy().reshape(-1), minlength=E)
+                                    for r in range(world)])
+            assert np.array_equal(counts, want_counts)
         assert pkg.device_status() == 0
         dist.barrier()
         (Path(result_dir) / f"ok{rank}").write_text("ok")

@@ -84,6 +84,49 @@ def test_regroup_plan_is_a_permutation_grouped_by_expert():
     assert empty.gather.size == 0 and empty.expert_offsets.tolist() == [0, 0, 0, 0]
 
 
+def test_peer_plan_moves_every_row_there_and_back():
+    """Simulate G GPUs in numpy: dispatch with send_dst_start, return with seg_start /
+    seg_home_row; every route's row must land in its expert's group and come home."""
+    ep = _pkg().moe_ep
+    rng = np.random.default_rng(3)
+    G, E, k, T = 4, 16, 3, 37
+    El = E // G
+    ids = [np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32) for _ in range(G)]
+    ids[1][:, 0] = 5  # skew: one hot expert
+    sorted_ = [moe_oracle.build_sorted_routes(ids[g], np.ones((T, k), np.float32), E, group=1) for g in range(G)]
+    counts = np.stack([s[5] for s in sorted_])
+    plans = [ep.peer_plan(counts, g) for g in range(G)]
+    cap = T * k * G
+    recv = [np.full((cap, 3), -1, dtype=np.int64) for _ in range(G)]  # payload: (src gpu, src pos, expert)
+    for g in range(G):
+        tok_ids, _, row_expert, nv, off, cnt, _ = sorted_[g]
+        for pos in range(int(nv[0])):
+            e = int(row_expert[pos])
+            dst = int(plans[g].send_dst_start[e]) + pos - int(off[e])
+            assert (recv[e // El][dst] == -1).all(), "two rows landed on one slot"
+            recv[e // El][dst] = (g, pos, e)
+    for g in range(G):
+        p = plans[g]
+        total = int(p.local_offsets[-1])
+        assert total == int(counts[:, g * El:(g + 1) * El].sum())
+        assert (recv[g][:total, 0] >= 0).all() and (recv[g][total:, 0] == -1).all()
+        for le in range(El):  # grouped by expert, sources in rank order
+            a, n = int(p.local_offsets[le]), int(p.local_counts[le])
+            assert (recv[g][a:a + n, 2] == g * El + le).all()
+            assert (np.diff(recv[g][a:a + n, 0]) >= 0).all()
+        # return trip
+        for row in range(total):
+            kseg = int(np.searchsorted(p.seg_start, row, side="right")) - 1
+            src = kseg % G
+            home = int(p.seg_home_row[kseg]) + row - int(p.seg_start[kseg])
+            assert recv[g][row, 0] == src and recv[g][row, 1] == home
+    # the two formulations of the grouped layout agree
+    for g in range(G):
+        rp = ep.regroup_plan(counts[:, g * El:(g + 1) * El])
+        assert np.array_equal(rp.expert_offsets, plans[g].local_offsets)
+        assert np.array_equal(rp.expert_counts, plans[g].local_counts)
+
+
 # ------------------------------------------------------------------ expert parallel over gloo
 class OracleOps:
     """Stand-in arithmetic for ExpertParallelMoE: the CPU oracle (test infrastructure)."""
