@@ -108,6 +108,18 @@ size_t lumen_b200_gemm_static_scratch_limit(void);
 int lumen_b200_fa_fwd_bf16(const void* Q, const void* K, const void* V, void* O, int B, int S,
                            int Hq, int Hkv, int D, float scale, int causal, void* stream);
 
+/* The same forward over variable-length sequences packed along the token dimension:
+ * Q,O [total_tokens,Hq,D], K,V [total_tokens,Hkv,D], seq_ptr int32 [num_seqs+1] prefix
+ * sums of the lengths (device pointer), max_seq_len = the longest sequence (sizes the
+ * grid).  This is the native calling convention of the reference kernel:
+ * flash_attn(q, k, v, seq_ptr, max_seq_len, out=)
+ * (datasets/inference/attention/lumen/attn_06_inst_scheduling.py:2144-2193), with
+ * seq_ptr built as at datasets/inference/attention/lumen/model.py:75-79. */
+int lumen_b200_fa_fwd_varlen_bf16(const void* Q, const void* K, const void* V, void* O,
+                                  const void* seq_ptr, int num_seqs, int total_tokens,
+                                  int max_seq_len, int Hq, int Hkv, int D, float scale, int causal,
+                                  void* stream);
+
 /* ------------------------------------------------------------------- MoE -- */
 
 /* logits[T,E] (fp32) = x[T,H] * wr[E,H]^T, bf16 inputs.  E * H * 2 bytes must fit

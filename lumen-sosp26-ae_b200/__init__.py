@@ -9,4 +9,4 @@ from . import _cabi  # noqa: F401
 from ._build import LIB_PATH, build_library, library_is_current  # noqa: F401
 from .gemm import clear_status, device_status, gemm_pipeline_transposed_b, gemm_workspace_bytes  # noqa: F401
 from . import attention, moe, moe_ep, sharding  # noqa: F401
-from .attention import flash_attn  # noqa: F401
+from .attention import flash_attn, flash_attn_packed  # noqa: F401

@@ -48,6 +48,11 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
          c_void_p],
     ),
+    "lumen_b200_fa_fwd_varlen_bf16": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_float, c_int, c_void_p],
+    ),
     "lumen_b200_moe_router_logits": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "lumen_b200_moe_route_topk": (

@@ -48,10 +48,11 @@ enum FaWaitCode {
 
 struct FaParams {
   __nv_bfloat16* O;
+  const int* seq_ptr;  // [B + 1] first packed row of each sequence, or nullptr: B sequences of S rows
   int B, S, Hq, Hkv;
   int causal;
   float scale_log2;  // scale * log2(e)
-  int q_blocks;      // ceil(S / 256)
+  int q_blocks;      // ceil(longest sequence / 256)
   int* status;
 };
 
@@ -93,16 +94,21 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int b = (blockIdx.x / prm.Hq) % prm.B;
   const int qb = prm.q_blocks - 1 - blockIdx.x / (prm.Hq * prm.B);
   const int hk = hq / (prm.Hq / prm.Hkv);
-  const int q0 = qb * 2 * kFaTile;  // first query row of tile 0
-  const int kv_tiles_all = (prm.S + kFaTile - 1) / kFaTile;
+  const int q0 = qb * 2 * kFaTile;  // first query row of tile 0 (within its sequence)
+  // Q, K, V, O are addressed as packed rows [sum of lengths, H, D]; sequence b owns rows
+  // [row_base, row_base + seq_len).  Keys past the end of a sequence are the next sequence's
+  // rows (or TMA zero fill at the very end): they are masked like any key beyond kv_lim.
+  const int row_base = prm.seq_ptr ? prm.seq_ptr[b] : b * prm.S;
+  const int seq_len = prm.seq_ptr ? prm.seq_ptr[b + 1] - row_base : prm.S;
+  const int kv_tiles_all = (seq_len + kFaTile - 1) / kFaTile;
   int n_tiles[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int row0 = q0 + t * kFaTile;
-    if (row0 >= prm.S) {
+    if (row0 >= seq_len) {
       n_tiles[t] = 0;
     } else if (prm.causal) {
-      const int last_row = min(row0 + kFaTile, prm.S) - 1;
+      const int last_row = min(row0 + kFaTile, seq_len) - 1;
       n_tiles[t] = min(kv_tiles_all, last_row / kFaTile + 1);
     } else {
       n_tiles[t] = kv_tiles_all;
@@ -149,8 +155,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int t = 0; t < 2; ++t) {
         if (n_tiles[t] == 0) continue;
         const uint32_t dst = smem_q + t * kFaTileBytes;
-        tma_load_4d(dst, &map_q, qbar, 0, hq, q0 + t * kFaTile, b);
-        tma_load_4d(dst + kFaHalfBytes, &map_q, qbar, 64, hq, q0 + t * kFaTile, b);
+        tma_load_3d(dst, &map_q, qbar, 0, hq, row_base + q0 + t * kFaTile);
+        tma_load_3d(dst + kFaHalfBytes, &map_q, qbar, 64, hq, row_base + q0 + t * kFaTile);
       }
       bool ok = true;
       for (int seq = 0; seq < 2 * n_max && ok; ++seq) {
@@ -163,10 +169,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const uint32_t bar = smem_u32(&tail->kv_full[slot]);
         const uint32_t dst = smem_kv + slot * kFaTileBytes;
         const CUtensorMap* map = (seq & 1) ? &map_v : &map_k;
-        const int row = (seq >> 1) * kFaTile;
+        const int row = row_base + (seq >> 1) * kFaTile;
         mbar_arrive_expect_tx(bar, kFaTileBytes);
-        tma_load_4d(dst, map, bar, 0, hk, row, b);
-        tma_load_4d(dst + kFaHalfBytes, map, bar, 64, hk, row, b);
+        tma_load_3d(dst, map, bar, 0, hk, row);
+        tma_load_3d(dst + kFaHalfBytes, map, bar, 64, hk, row);
       }
     }
   } else if (warp == 1) {
@@ -267,7 +273,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const uint32_t o_tmem = tmem_base + lane_sel + 256 + t * 128;
     const float sl2 = prm.scale_log2;
     // last key this row may see
-    const int kv_lim = prm.causal ? min(q, prm.S - 1) : prm.S - 1;
+    const int kv_lim = prm.causal ? min(q, seq_len - 1) : seq_len - 1;
 
     float m = -INFINITY;  // running maximum (raw score units)
     float l = 0.f;        // running sum of probabilities
@@ -375,13 +381,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tc_fence_after_sync();
         const float inv_l = 1.0f / l;
         __nv_bfloat16* orow =
-            prm.O + ((size_t(b) * prm.S + q) * prm.Hq + hq) * kFaD;
+            prm.O + ((size_t(row_base) + q) * prm.Hq + hq) * kFaD;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
           tmem_ld_32x32b_x32(o_tmem + c * 32, ov);
           tmem_ld_wait();
-          if (q < prm.S) {
+          if (q < seq_len) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               uint4 o;
@@ -415,26 +421,19 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
 using namespace b200;
 
-extern "C" int lumen_b200_fa_fwd_bf16(const void* Q, const void* K, const void* V, void* O, int B,
-                                       int S, int Hq, int Hkv, int D, float scale, int causal,
-                                       void* stream) {
-  if (!Q || !K || !V || !O || B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0) return LUMEN_B200_EINVAL;
-  if (D != kFaD) return LUMEN_B200_EUNSUPPORTED;
-  if (Hq % Hkv != 0 || !(scale > 0.f)) return LUMEN_B200_EINVAL;
-  if ((reinterpret_cast<uintptr_t>(Q) & 15) || (reinterpret_cast<uintptr_t>(K) & 15) ||
-      (reinterpret_cast<uintptr_t>(V) & 15) || (reinterpret_cast<uintptr_t>(O) & 15))
-    return LUMEN_B200_EINVAL;
+namespace {
+
+// rows = packed tokens; S_max = longest sequence (sizes the grid)
+int launch_fa(const void* Q, const void* K, const void* V, void* O, const int* seq_ptr, int B, int S_uniform,
+              long long rows, int S_max, int Hq, int Hkv, float scale, int causal, cudaStream_t st) {
   int* status = device_status_word();
   if (!status) return LUMEN_B200_ECUDA;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-
   auto make_map = [&](CUtensorMap* map, const void* base, int heads) {
-    // [B, S, H, D] contiguous, innermost first: D, H, S, B; box = 64 x 1 x 128 x 1
-    const uint64_t dims[4] = {uint64_t(kFaD), uint64_t(heads), uint64_t(S), uint64_t(B)};
-    const uint64_t strides[3] = {uint64_t(kFaD) * 2, uint64_t(heads) * kFaD * 2,
-                                 uint64_t(S) * heads * kFaD * 2};
-    const uint32_t box[4] = {64, 1, uint32_t(kFaTile), 1};
-    return encode_tmap_bf16(map, base, 4, dims, strides, box);
+    // [rows, H, D] contiguous, innermost first: D, H, rows; box = 64 x 1 x 128
+    const uint64_t dims[3] = {uint64_t(kFaD), uint64_t(heads), uint64_t(rows)};
+    const uint64_t strides[2] = {uint64_t(kFaD) * 2, uint64_t(heads) * kFaD * 2};
+    const uint32_t box[3] = {64, 1, uint32_t(kFaTile)};
+    return encode_tmap_bf16(map, base, 3, dims, strides, box);
   };
   CUtensorMap mq, mk, mv;
   if (make_map(&mq, Q, Hq) != 0 || make_map(&mk, K, Hkv) != 0 || make_map(&mv, V, Hkv) != 0)
@@ -442,13 +441,14 @@ extern "C" int lumen_b200_fa_fwd_bf16(const void* Q, const void* K, const void* 
 
   FaParams prm{};
   prm.O = static_cast<__nv_bfloat16*>(O);
+  prm.seq_ptr = seq_ptr;
   prm.B = B;
-  prm.S = S;
+  prm.S = S_uniform;
   prm.Hq = Hq;
   prm.Hkv = Hkv;
   prm.causal = causal ? 1 : 0;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.q_blocks = (S + 2 * kFaTile - 1) / (2 * kFaTile);
+  prm.q_blocks = (S_max + 2 * kFaTile - 1) / (2 * kFaTile);
   prm.status = status;
 
   constexpr int kSlots = 4;
@@ -464,7 +464,36 @@ extern "C" int lumen_b200_fa_fwd_bf16(const void* Q, const void* K, const void* 
     configured[dev] = true;
   }
   const long long grid = static_cast<long long>(prm.q_blocks) * B * Hq;
-  if (grid > 0x7fffffffLL) return LUMEN_B200_EUNSUPPORTED;
+  if (grid <= 0 || grid > 0x7fffffffLL) return LUMEN_B200_EUNSUPPORTED;
   kern<<<static_cast<unsigned>(grid), kFaThreads, smem, st>>>(mq, mk, mv, prm);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" int lumen_b200_fa_fwd_bf16(const void* Q, const void* K, const void* V, void* O, int B,
+                                       int S, int Hq, int Hkv, int D, float scale, int causal,
+                                       void* stream) {
+  if (!Q || !K || !V || !O || B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0) return LUMEN_B200_EINVAL;
+  if (D != kFaD) return LUMEN_B200_EUNSUPPORTED;
+  if (Hq % Hkv != 0 || !(scale > 0.f)) return LUMEN_B200_EINVAL;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return LUMEN_B200_EINVAL;
+  return launch_fa(Q, K, V, O, nullptr, B, S, static_cast<long long>(B) * S, S, Hq, Hkv, scale, causal,
+                   static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lumen_b200_fa_fwd_varlen_bf16(const void* Q, const void* K, const void* V, void* O,
+                                              const void* seq_ptr, int num_seqs, int total_tokens,
+                                              int max_seq_len, int Hq, int Hkv, int D, float scale,
+                                              int causal, void* stream) {
+  if (!Q || !K || !V || !O || !seq_ptr || num_seqs <= 0 || total_tokens <= 0 || max_seq_len <= 0 ||
+      Hq <= 0 || Hkv <= 0)
+    return LUMEN_B200_EINVAL;
+  if (D != kFaD) return LUMEN_B200_EUNSUPPORTED;
+  if (Hq % Hkv != 0 || !(scale > 0.f) || max_seq_len > total_tokens) return LUMEN_B200_EINVAL;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return LUMEN_B200_EINVAL;
+  return launch_fa(Q, K, V, O, static_cast<const int*>(seq_ptr), num_seqs, 0, total_tokens, max_seq_len, Hq,
+                   Hkv, scale, causal, static_cast<cudaStream_t>(stream));
 }

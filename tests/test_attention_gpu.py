@@ -114,3 +114,44 @@ def test_full_size_configs_sampled(cuda_pkg, name, B, S, Hq, Hkv, causal):
             scores = scores.masked_fill(torch.arange(S).unsqueeze(0) > rows.unsqueeze(1), float("-inf"))
         want = torch.softmax(scores, dim=-1) @ vf
         torch.testing.assert_close(out[b, rows, h].cpu().float(), want, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("lengths,Hq,Hkv", [
+    ([5, 300, 1, 128, 257], 8, 1),      # the reference's head layout, ragged lengths
+    ([1000, 24, 640], 4, 2),
+    ([128, 128], 2, 2),
+])
+@pytest.mark.parametrize("causal", [True, False])
+def test_packed_variable_length(cuda_pkg, lengths, Hq, Hkv, causal):
+    """flash_attn(q, k, v, seq_ptr, max_seq_len): every sequence equals the oracle run on it alone."""
+    total = sum(lengths)
+    g = torch.Generator().manual_seed(total + Hq)
+    q = torch.randn((total, Hq, 128), generator=g).to(torch.bfloat16)
+    k = torch.randn((total, Hkv, 128), generator=g).to(torch.bfloat16)
+    v = torch.randn((total, Hkv, 128), generator=g).to(torch.bfloat16)
+    seq_ptr = torch.tensor([0] + list(torch.tensor(lengths).cumsum(0)), dtype=torch.int32)
+    out = cuda_pkg.flash_attn_packed(q.to(DEV), k.to(DEV), v.to(DEV), seq_ptr.to(DEV), max(lengths), causal=causal)
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    out = out.cpu()
+    for i, n in enumerate(lengths):
+        a = int(seq_ptr[i])
+        want = attention_oracle.attention_reference(q[a:a + n].unsqueeze(0), k[a:a + n].unsqueeze(0),
+                                                    v[a:a + n].unsqueeze(0), causal=causal)[0]
+        torch.testing.assert_close(out[a:a + n].float(), want.float(), rtol=RTOL, atol=ATOL)
+
+
+def test_packed_matches_batched_layout(cuda_pkg):
+    """The harness layout [B,S,H,D] is the packed layout with seq_ptr = arange(B+1) * S
+    (datasets/inference/attention/lumen/model.py:64-79 of the reference): identical bits."""
+    q, k, v = attention_oracle.attention_inputs(3, 200, 8, 2, 128, 21)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    a = cuda_pkg.flash_attn(qd, kd, vd, causal=True)
+    seq_ptr = (torch.arange(4, dtype=torch.int32) * 200).to(DEV)
+    b = cuda_pkg.flash_attn_packed(qd.view(600, 8, 128), kd.view(600, 2, 128), vd.view(600, 2, 128), seq_ptr, 200)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(600, 8, 128), b)
+    with pytest.raises(TypeError):
+        cuda_pkg.flash_attn_packed(qd.view(600, 8, 128), kd.view(600, 2, 128), vd.view(600, 2, 128), [0, 600], 600)
+    with pytest.raises(ValueError, match="cannot exceed total_tokens"):
+        cuda_pkg.flash_attn_packed(qd.view(600, 8, 128), kd.view(600, 2, 128), vd.view(600, 2, 128), seq_ptr, 601)
