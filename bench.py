@@ -100,7 +100,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sm, smax, reasons = [], [], set()
+        sm, smax, power, reasons = [], [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in self.lines:
             parts = [x.strip() for x in line.split(",")]
@@ -109,16 +109,18 @@ class ClockSampler:
             try:
                 sm.append(float(parts[1]))
                 smax.append(float(parts[2]))
+                power.append(float(parts[3]))
             except ValueError:
                 continue
             for name, val in zip(names, parts[4:8]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
-        # the region of interest is the loaded part: keep the upper half of the samples
-        loaded = sorted(sm)[len(sm) // 2:] if sm else []
+        # "under load" = samples drawing at least half of the highest power seen
+        top = max(power) if power else 0.0
+        loaded = [c for c, w in zip(sm, power) if w >= 0.5 * top] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "sm_max_mhz": max(smax) if smax else None, "power_w_max": top or None,
+                "samples": len(sm), "samples_under_load": len(loaded), "reasons": sorted(reasons)}
 
 
 # --------------------------------------------------------------------------- CPU arm
