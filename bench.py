@@ -560,7 +560,8 @@ def run_ep_case(args) -> None:
         w13[e] = randn_bf16((2 * I, H), 0.02)
         w2[e] = randn_bf16((H, I), 0.02)
     if args.transport == "peer":
-        ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=Tl, hidden=H, inter=I, experts=E, topk=K, device=dev)
+        ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=Tl, hidden=H, inter=I, experts=E, topk=K, device=dev,
+                                              fused_return=args.fused_return)
     else:
         ops = pkg.moe_ep.CudaOps(dev, tokens_global=T, experts=E, topk=K)
         ep = pkg.moe_ep.ExpertParallelMoE(experts=E, topk=K, ops=ops)
@@ -615,6 +616,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--transport", choices=("peer", "nccl"), default="peer",
                     help="--case ep:*: how rows cross GPUs")
+    ap.add_argument("--fused-return", action="store_true",
+                    help="--case ep:* --transport peer: the second expert GEMM's epilogue stores rows to their home GPU")
     ap.add_argument("--eager", action="store_true", help="--case: time eager launches instead of graph replays")
     ap.add_argument("--case", default=None, help="run one operator case instead of the sweep (see run_case)")
     args = ap.parse_args()

@@ -180,6 +180,19 @@ int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights, void* out
                                 int max_rows, int E, int N, int K, int gated, int rows_hint,
                                 void* stream);
 
+/* The same per-expert GEMM with its output rows scattered: row r is written at
+ * out_row_ptrs[r] (device array of max_rows device pointers; nullptr = do not store),
+ * which may point into a peer GPU's memory.  With the table of
+ * lumen_b200_moe_ep_row_ptrs the epilogue of the second expert GEMM is the return trip of
+ * the expert-parallel exchange: each tile's rows leave for their home GPU as soon as the
+ * tile is done.  Fuses what the reference's single-GPU kernel does with atomics in
+ * _stage2_write_back (datasets/inference/moe/lumen/fused_moe.py:864-888). */
+int lumen_b200_moe_grouped_gemm_to_rows(const void* acts, const void* weights,
+                                        const void* const* out_row_ptrs,
+                                        const void* expert_offsets, const void* expert_counts,
+                                        int max_rows, int E, int N, int K, int gated,
+                                        int rows_hint, void* stream);
+
 /* out[t,:] = sum_slot topk_weights[t,slot] * y[route_pos[t*k+slot],:], fp32 sum in
  * slot order, bf16 out.  Replaces the atomic write-back of _stage2_write_back
  * (datasets/inference/moe/lumen/fused_moe.py:864-888) with a deterministic gather. */
@@ -219,6 +232,13 @@ int lumen_b200_moe_ep_dispatch(const void* x, const void* sorted_token_ids, cons
 int lumen_b200_moe_ep_return(const void* y, const void* seg_start, const void* seg_home_row,
                              const void* const* peer_buffers, int G, int El, int H, int max_rows,
                              int home_capacity_rows, void* stream);
+
+/* row_ptrs[g] (max_rows device pointers) = home address of grouped output row g: GPU
+ * k % G, row seg_home_row[k] + (g - seg_start[k]) for the segment k that holds g; nullptr
+ * past the last segment.  Input of lumen_b200_moe_grouped_gemm_to_rows. */
+int lumen_b200_moe_ep_row_ptrs(const void* seg_start, const void* seg_home_row,
+                               const void* const* peer_buffers, int G, int El, int H, int max_rows,
+                               int home_capacity_rows, void* row_ptrs, void* stream);
 
 #ifdef __cplusplus
 }

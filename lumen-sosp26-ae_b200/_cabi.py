@@ -82,6 +82,16 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_int, c_int,
          c_void_p],
     ),
+    "lumen_b200_moe_grouped_gemm_to_rows": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_void_p],
+    ),
+    "lumen_b200_moe_ep_row_ptrs": (
+        c_int,
+        [c_void_p, c_void_p, ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_int, c_int, c_void_p,
+         c_void_p],
+    ),
     "lumen_b200_moe_combine": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
 }

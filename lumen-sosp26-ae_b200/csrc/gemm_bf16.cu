@@ -200,11 +200,34 @@ extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, in
   }
 }
 
+static int grouped_gemm_impl(const void* acts, const void* weights, void* out, const void* const* out_row_ptrs,
+                             const void* expert_offsets, const void* expert_counts, int max_rows, int E,
+                             int N, int K, int gated, int rows_hint, void* stream);
+
 extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights, void* out,
                                             const void* expert_offsets, const void* expert_counts,
                                             int max_rows, int E, int N, int K, int gated,
                                             int rows_hint, void* stream) {
-  if (!acts || !weights || !out || !expert_offsets || !expert_counts) return LUMEN_B200_EINVAL;
+  if (!out) return LUMEN_B200_EINVAL;
+  return grouped_gemm_impl(acts, weights, out, nullptr, expert_offsets, expert_counts, max_rows, E, N, K,
+                           gated, rows_hint, stream);
+}
+
+extern "C" int lumen_b200_moe_grouped_gemm_to_rows(const void* acts, const void* weights,
+                                                    const void* const* out_row_ptrs,
+                                                    const void* expert_offsets,
+                                                    const void* expert_counts, int max_rows, int E,
+                                                    int N, int K, int gated, int rows_hint,
+                                                    void* stream) {
+  if (!out_row_ptrs) return LUMEN_B200_EINVAL;
+  return grouped_gemm_impl(acts, weights, nullptr, out_row_ptrs, expert_offsets, expert_counts, max_rows, E,
+                           N, K, gated, rows_hint, stream);
+}
+
+static int grouped_gemm_impl(const void* acts, const void* weights, void* out, const void* const* out_row_ptrs,
+                             const void* expert_offsets, const void* expert_counts, int max_rows, int E,
+                             int N, int K, int gated, int rows_hint, void* stream) {
+  if (!acts || !weights || !expert_offsets || !expert_counts) return LUMEN_B200_EINVAL;
   if (max_rows <= 0 || E <= 0 || E > kMaxExperts || N <= 0 || K <= 0 || K % 8 != 0)
     return LUMEN_B200_EINVAL;
   if ((reinterpret_cast<uintptr_t>(acts) & 15) || (reinterpret_cast<uintptr_t>(weights) & 15))
@@ -227,6 +250,7 @@ extern "C" int lumen_b200_moe_grouped_gemm(const void* acts, const void* weights
   args.num_experts = E;
   args.w_rows_per_expert = w_rows;
   args.up_row_offset = N;
+  args.out_row_ptrs = reinterpret_cast<__nv_bfloat16* const*>(const_cast<void* const*>(out_row_ptrs));
   args.status = status;
 
   const uint64_t w_total_rows = uint64_t(E) * w_rows;

@@ -51,6 +51,10 @@ struct GemmArgs {
   int num_experts;
   int w_rows_per_expert;  // rows of the stacked weight tensor per expert
   int up_row_offset;      // gated: distance from a gate row to its up row
+  // grouped, optional: where each output row lives.  out_row_ptrs[r] is the address of the
+  // first element of output row r (possibly in a peer GPU's memory: the epilogue then is the
+  // send of the expert-parallel return trip) or nullptr for a row that must not be stored.
+  __nv_bfloat16* const* out_row_ptrs;
   int* status;
 };
 
@@ -388,9 +392,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
       if constexpr (!SWAP) {
         // thread p owns output row out_row + p; 32-column chunks
-        const bool row_ok = p < t.rows_valid;
-        __nv_bfloat16* orow = args.out + size_t(t.out_row + p) * args.ldo + t.out_col;
-        const bool vec_ok = (args.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
+        bool row_ok = p < t.rows_valid;
+        __nv_bfloat16* orow;
+        bool vec_ok;
+        if (GROUPED && args.out_row_ptrs) {
+          __nv_bfloat16* base = row_ok ? args.out_row_ptrs[t.out_row + p] : nullptr;
+          row_ok = base != nullptr;
+          orow = base + t.out_col;
+          vec_ok = (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+        } else {
+          orow = args.out + size_t(t.out_row + p) * args.ldo + t.out_col;
+          vec_ok = (args.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
+        }
         constexpr int kChunks = Cfg::kOutCols / 32;
 #pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
@@ -479,8 +492,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j = 0; j < kChunkCols; ++j) {
               const int r = c * 32 + j;
-              if (r < t.rows_valid)
-                args.out[size_t(t.out_row + r) * args.ldo + t.out_col + p] = __float2bfloat16_rn(f[j]);
+              if (r < t.rows_valid) {
+                if (GROUPED && args.out_row_ptrs) {
+                  __nv_bfloat16* base = args.out_row_ptrs[t.out_row + r];
+                  if (base) base[t.out_col + p] = __float2bfloat16_rn(f[j]);
+                } else {
+                  args.out[size_t(t.out_row + r) * args.ldo + t.out_col + p] = __float2bfloat16_rn(f[j]);
+                }
+              }
             }
           }
         }

@@ -620,7 +620,54 @@ __global__ void __launch_bounds__(256)
   __threadfence_system();
 }
 
+// Address of every grouped output row on its way home: row g of segment k goes to GPU
+// k % G, row seg_home_row[k] + (g - seg_start[k]).  Rows past the last segment get nullptr.
+__global__ void __launch_bounds__(256)
+    moe_ep_row_ptrs_kernel(const int* __restrict__ seg_start, const int* __restrict__ seg_home_row,
+                           PeerPtrs peers, int H, int G, int nseg, int home_capacity_rows, int max_rows,
+                           __nv_bfloat16** __restrict__ row_ptrs, int* status) {
+  const int total = seg_start[nseg];
+  for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < max_rows; g += gridDim.x * blockDim.x) {
+    __nv_bfloat16* ptr = nullptr;
+    if (g < total) {
+      int lo = 0, hi = nseg;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (seg_start[mid] <= g) lo = mid; else hi = mid;
+      }
+      const int dst_row = seg_home_row[lo] + (g - seg_start[lo]);
+      if (dst_row >= 0 && dst_row < home_capacity_rows)
+        ptr = static_cast<__nv_bfloat16*>(peers.p[lo % G]) + size_t(dst_row) * H;
+      else
+        atomicCAS(status, 0, (34 << 16) | (blockIdx.x & 0xffff));
+    }
+    row_ptrs[g] = ptr;
+  }
+}
+
 }  // namespace b200
+
+extern "C" int lumen_b200_moe_ep_row_ptrs(const void* seg_start, const void* seg_home_row,
+                                           const void* const* peer_buffers, int G, int El, int H,
+                                           int max_rows, int home_capacity_rows, void* row_ptrs,
+                                           void* stream) {
+  if (!seg_start || !seg_home_row || !peer_buffers || !row_ptrs) return LUMEN_B200_EINVAL;
+  if (G <= 0 || G > kMaxEpRanks || El <= 0 || H <= 0 || H % 8 != 0 || max_rows <= 0 ||
+      home_capacity_rows <= 0)
+    return LUMEN_B200_EINVAL;
+  PeerPtrs peers{};
+  for (int g = 0; g < G; ++g) {
+    if (!peer_buffers[g] || (reinterpret_cast<uintptr_t>(peer_buffers[g]) & 15)) return LUMEN_B200_EINVAL;
+    peers.p[g] = const_cast<void*>(peer_buffers[g]);
+  }
+  int* status = device_status_word();
+  if (!status) return LUMEN_B200_ECUDA;
+  const int grid = (max_rows + 255) / 256;
+  moe_ep_row_ptrs_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const int*>(seg_start), static_cast<const int*>(seg_home_row), peers, H, G, El * G,
+      home_capacity_rows, max_rows, static_cast<__nv_bfloat16**>(row_ptrs), status);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
 
 extern "C" int lumen_b200_moe_ep_plan(const void* counts, int G, int E, int rank, void* send_dst_start,
                                        void* local_offsets, void* local_counts, void* seg_start,

@@ -206,6 +206,27 @@ def grouped_gemm(acts: torch.Tensor, weights: torch.Tensor, routes: SortedRoutes
     return out
 
 
+def grouped_gemm_to_rows(acts: torch.Tensor, weights: torch.Tensor, row_ptrs: torch.Tensor, routes, *,
+                         gated: bool, rows_hint: int) -> None:
+    """grouped_gemm whose output row r is written at the address row_ptrs[r] (int64 device
+    tensor of addresses, 0 = skip); the addresses may lie in a peer GPU's memory."""
+    dev = _need_cuda(acts, weights, row_ptrs)
+    if row_ptrs.dtype != torch.int64:
+        raise ValueError("row_ptrs must be an int64 tensor of device addresses")
+    P, K = acts.shape
+    E, w_rows, K2 = weights.shape
+    if K2 != K:
+        raise ValueError(f"weights K ({K2}) must equal activations K ({K}).")
+    if row_ptrs.numel() < P:
+        raise ValueError("row_ptrs must have one entry per activation row")
+    N = w_rows // 2 if gated else w_rows
+    with _cabi.on_device(dev):
+        rc = _cabi.load().lumen_b200_moe_grouped_gemm_to_rows(
+            acts.data_ptr(), weights.data_ptr(), row_ptrs.data_ptr(), routes.expert_offsets.data_ptr(),
+            routes.expert_counts.data_ptr(), P, E, N, K, 1 if gated else 0, int(rows_hint), _stream(dev))
+    _cabi.check("lumen_b200_moe_grouped_gemm_to_rows", rc)
+
+
 def combine(y: torch.Tensor, routes: SortedRoutes, topk_weights: torch.Tensor, tokens: int,
             out: torch.Tensor | None = None) -> torch.Tensor:
     dev = _need_cuda(y, topk_weights)
