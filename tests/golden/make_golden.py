@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory from the REFERENCE's own code.
 
-Run in a container that has the reference checkout (default /root/reference):
+Run where a checkout of the reference exists:
 
-    python tests/golden/make_golden.py [--reference /path/to/lumen-sosp26-ae]
+    python tests/golden/make_golden.py --reference /path/to/lumen-sosp26-ae
 
 It imports, unmodified,
   * prompts/kernelbench/1_gemm.py            Model
@@ -51,7 +51,7 @@ def max_ulp_bf16(a: torch.Tensor, b: torch.Tensor) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of haohui/lumen-sosp26-ae")
     ref = Path(ap.parse_args().reference)
     sys.path.insert(0, str(ref / "scripts" / "benchmark"))
     torch.manual_seed(0)
