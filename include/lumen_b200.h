@@ -199,6 +199,13 @@ int lumen_b200_moe_grouped_gemm_to_rows(const void* acts, const void* weights,
 int lumen_b200_moe_combine(const void* y, const void* route_pos, const void* topk_weights,
                            void* out, int T, int H, int k, void* stream);
 
+/* out[T,H] (bf16) = lut[q[t,h]] * scale[t, h/128]: fp8 activations (one byte each) with
+ * per-128-element fp32 scales to bf16.  lut = 256 floats, the value of every fp8 code
+ * (covers e4m3fn and e4m3fnuz).  H % 128 == 0.  Stands in for the activation dequantisation
+ * the reference folds into its MFMA loop (datasets/inference/moe/lumen/fused_moe.py:400-443). */
+int lumen_b200_moe_dequant_fp8(const void* q, const void* scale, const void* lut, void* out, int T,
+                               int H, void* stream);
+
 /* ---------------------------------------------- MoE, expert parallel (G GPUs) -- */
 /* Tokens and experts are sharded over G GPUs (expert e on GPU e / (E/G)); each GPU sorts
  * its own routes compactly (route_group = 1).  `counts` is the G x E matrix of every

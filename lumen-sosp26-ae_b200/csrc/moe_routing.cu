@@ -470,6 +470,54 @@ extern "C" int lumen_b200_moe_combine(const void* y, const void* route_pos, cons
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
 
+// ---------------------------------------------------------------------------
+// fp8 activations with per-128-element scales -> bf16 (the harness' default storage
+// format, scripts/benchmark/backend_moe.py:86-147 of the reference).  The 256-entry
+// table holds the float value of every fp8 code, so e4m3fn and e4m3fnuz are both covered.
+// out[t][h] = lut[q[t][h]] * scale[t][h / 128]; 16 elements per thread.
+// ---------------------------------------------------------------------------
+namespace b200 {
+__global__ void __launch_bounds__(256)
+    moe_dequant_fp8_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
+                           const float* __restrict__ lut, __nv_bfloat16* __restrict__ out, int T, int H) {
+  __shared__ float s_lut[256];
+  s_lut[threadIdx.x] = lut[threadIdx.x];
+  __syncthreads();
+  const int chunks_per_row = H / 16;
+  const long long total = static_cast<long long>(T) * chunks_per_row;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / chunks_per_row);
+    const int c = static_cast<int>(i - static_cast<long long>(t) * chunks_per_row);
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(q + static_cast<size_t>(t) * H) + c);
+    const float sc = __ldg(scale + static_cast<size_t>(t) * (H / 128) + (c * 16) / 128);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+    uint32_t packed[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      packed[j] = pack_bf16x2(s_lut[b[2 * j]] * sc, s_lut[b[2 * j + 1]] * sc);
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c * 16);
+    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  }
+}
+}  // namespace b200
+
+extern "C" int lumen_b200_moe_dequant_fp8(const void* q, const void* scale, const void* lut, void* out, int T,
+                                           int H, void* stream) {
+  if (!q || !scale || !lut || !out || T <= 0 || H <= 0 || H % 128 != 0) return LUMEN_B200_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return LUMEN_B200_EINVAL;
+  const int sms = b200::device_sm_count();
+  if (sms <= 0) return LUMEN_B200_ECUDA;
+  const long long total = static_cast<long long>(T) * (H / 16);
+  long long grid = (total + 255) / 256;
+  if (grid > sms * 16) grid = sms * 16;
+  b200::moe_dequant_fp8_kernel<<<static_cast<unsigned>(grid), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(q), static_cast<const float*>(scale), static_cast<const float*>(lut),
+      static_cast<__nv_bfloat16*>(out), T, H);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
 // ===========================================================================
 // Expert-parallel dispatch and return over peer memory (NVLink / NVSwitch).
 //

@@ -6,10 +6,12 @@
 `Model(variant=...).build_cases(...)` follows the case-backend contract
 (scripts/benchmark/backend_moe.py:263-336): it receives the harness' precomputed routing
 (topk_ids, topk_weights) and returns zero-argument callables.  `ModelNew.forward` follows
-the python-backend contract (:339-403).  The harness' block scales (input_scale,
-fc1_scale, fc2_scale) are folded into bf16 copies of the activations and weights once,
-outside the timed call, the way the reference's Lumen system pre-shuffles its weights
-(datasets/inference/moe/lumen/model.py:184-199); with unit scales nothing is copied.
+the python-backend contract (:339-403).  The expert GEMMs compute in bf16.  The harness'
+weight block scales (fc1_scale, fc2_scale) and, for fp8 storage, the fp8 codes are folded
+into bf16 copies of the weights once, outside the timed call, the way the reference's Lumen
+system pre-shuffles its weights (datasets/inference/moe/lumen/model.py:184-199) and its
+ksearch system caches dequantised weights (datasets/inference/moe/ksearch/main.cpp:23-37);
+fp8 activations are dequantised by a kernel inside every call.
 """
 from __future__ import annotations
 
@@ -31,8 +33,8 @@ BLOCK = 128
 
 
 def _fold_block_scale(w: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
-    """w [E, rows, cols] bf16 times scale [E, (rows/128)*(cols/128)] -> bf16."""
-    if bool(torch.all(scale == 1.0)):
+    """w [E, rows, cols] (bf16 or fp8) times scale [E, (rows/128)*(cols/128)] -> bf16."""
+    if w.dtype == torch.bfloat16 and bool(torch.all(scale == 1.0)):
         return w
     E, rows, cols = w.shape
     s = scale.to(torch.float32).view(E, rows // BLOCK, 1, cols // BLOCK, 1)
@@ -67,8 +69,8 @@ class Model:
     def build_cases(self, *, seq_len: int, shared_input: Any, shared_weights: dict[str, torch.Tensor],
                     dim: int, inter_dim: int, experts: int, topk: int,
                     input_dtype: str) -> List[Callable[[], torch.Tensor]]:
-        if input_dtype != "bf16":
-            raise ValueError("B200 MoE supports only bf16 input")
+        if input_dtype not in ("bf16", "fp8"):
+            raise ValueError("B200 MoE supports bf16 and fp8 input")
         x = shared_input
         for name in ("input_q", "topk_weights", "topk_ids", "input_scale"):
             if not hasattr(x, name):
@@ -80,8 +82,11 @@ class Model:
         w13, w2 = self._prepare_weights(shared_weights)
         if tuple(w13.shape) != (experts, inter_dim * 2, dim):
             raise ValueError(f"w1_q shape mismatch: expected {(experts, inter_dim * 2, dim)}, got {tuple(w13.shape)}")
-        xin = _fold_input_scale(x.input_q, x.input_scale)
-        dev = xin.device
+        fp8_in = x.input_q.dtype != torch.bfloat16
+        # fp8 activations are dequantised by a kernel inside the timed call (they arrive as
+        # fp8); bf16 activations with non-unit scales are folded once here
+        xin = None if fp8_in else _fold_input_scale(x.input_q, x.input_scale)
+        dev = x.input_q.device
         key = (seq_len, dim, inter_dim, experts, topk, dev)
         op = self._ops.get(key)
         if op is None:
@@ -91,8 +96,16 @@ class Model:
         ids = x.topk_ids.to(torch.int32).contiguous()
         wts = x.topk_weights.to(torch.float32).contiguous()
 
-        def run_b200() -> torch.Tensor:
-            return op.forward_routed(xin, ids, wts, w13, w2)
+        if fp8_in:
+            xq, xscale = x.input_q.contiguous(), x.input_scale.to(torch.float32).contiguous()
+            xbuf = torch.empty((seq_len, dim), dtype=torch.bfloat16, device=dev)
+
+            def run_b200() -> torch.Tensor:
+                _moe.dequant_fp8_rows(xq, xscale, out=xbuf)
+                return op.forward_routed(xbuf, ids, wts, w13, w2)
+        else:
+            def run_b200() -> torch.Tensor:
+                return op.forward_routed(xin, ids, wts, w13, w2)
 
         return [run_b200]
 
@@ -115,7 +128,7 @@ class ModelNew(nn.Module):
         weights = {"w1_q": w1_q, "w2_q": w2_q, "fc1_scale": fc1_scale, "fc2_scale": fc2_scale}
         return self._impl.build_cases(seq_len=T, shared_input=s, shared_weights=weights, dim=H,
                                       inter_dim=two_i // 2, experts=E, topk=topk_ids.shape[1],
-                                      input_dtype="bf16")[0]()
+                                      input_dtype="bf16" if input_q.dtype == torch.bfloat16 else "fp8")[0]()
 
 
 DIM = 4096

@@ -1,8 +1,7 @@
 #!/usr/bin/env python3
-"""Fused-MoE benchmark (bf16 storage, precomputed top-k routing), CUDA-graph timing.
+"""Fused-MoE benchmark (bf16 or fp8 storage, precomputed top-k routing), CUDA-graph timing.
 
-Same flags and JSONL record as the reference's scripts/benchmark/bench_moe.py with
---input-dtype bf16: inputs and weights follow backend_moe.py:86-210 (x = randn + 0.1, positive
+Same flags and JSONL record as the reference's scripts/benchmark/bench_moe.py: inputs and weights follow backend_moe.py:86-210 (x = randn + 0.1, positive
 per-128-block scales, scores ~ N(0,1) -> topk(sorted) -> softmax of the k values; weights from
 seed + 17, randn * 8, positive block scales), the check is the routed fp32 reference of
 :469-525 with its tolerance (:22-25), and a backend is a `Model(variant=).build_cases(...)`."""
@@ -24,11 +23,19 @@ TOL = 1e-1
 TOKENS = [1024, 2048, 4096, 8192, 16384]
 
 
-def make_inputs(tokens, dim, experts, topk, dev, seed):
+def fp8_dtype():
+    """The harness picks e4m3fnuz when torch has it, else e4m3fn (backend_moe.py:65-73)."""
+    dt = getattr(torch, "float8_e4m3fnuz", None) or getattr(torch, "float8_e4m3fn", None)
+    if dt is None:
+        raise RuntimeError("torch float8 dtype is unavailable")
+    return dt
+
+
+def make_inputs(tokens, dim, experts, topk, dev, seed, dtype=torch.bfloat16):
     gen = torch.Generator(device=dev).manual_seed(seed)
     out = {}
     for t in tokens:
-        x = torch.randn((t, dim), dtype=torch.float32, device=dev, generator=gen).add_(0.1).to(torch.bfloat16)
+        x = torch.randn((t, dim), dtype=torch.float32, device=dev, generator=gen).add_(0.1).to(dtype)
         xs = torch.randn((t, dim // BLOCK), dtype=torch.float32, device=dev, generator=gen).mul_(2e-2).add_(1e-1)
         scores = torch.randn((t, experts), dtype=torch.float32, device=dev, generator=gen)
         val, idx = torch.topk(scores, k=topk, dim=-1, largest=True, sorted=True)
@@ -38,14 +45,14 @@ def make_inputs(tokens, dim, experts, topk, dev, seed):
     return out
 
 
-def make_weights(dim, inter, experts, dev, seed):
+def make_weights(dim, inter, experts, dev, seed, dtype=torch.bfloat16):
     gen = torch.Generator(device=dev).manual_seed(seed + 17)
 
     def rnd(shape):
         return torch.randn(shape, dtype=torch.float32, device=dev, generator=gen)
 
-    w1 = rnd((experts, 2 * inter, dim)).mul_(8.0).to(torch.bfloat16)
-    w2 = rnd((experts, dim, inter)).mul_(8.0).to(torch.bfloat16)
+    w1 = rnd((experts, 2 * inter, dim)).mul_(8.0).to(dtype)
+    w2 = rnd((experts, dim, inter)).mul_(8.0).to(dtype)
     s1 = rnd((experts, (2 * inter // BLOCK) * (dim // BLOCK))).mul_(2e-3).add_(1e-2).clamp_min_(1e-8)
     s2 = rnd((experts, (dim // BLOCK) * (inter // BLOCK))).mul_(2e-3).add_(1e-2).clamp_min_(1e-8)
     return {"w1_q": w1.contiguous(), "w2_q": w2.contiguous(), "fc1_scale": s1.contiguous(), "fc2_scale": s2.contiguous()}
@@ -90,7 +97,7 @@ def run(argv=None) -> list[dict]:
     p.add_argument("--inter-dim", type=int, default=2048)
     p.add_argument("--experts", type=int, default=32)
     p.add_argument("--topk", type=int, default=4)
-    p.add_argument("--input-dtype", choices=["bf16"], default="bf16")
+    p.add_argument("--input-dtype", choices=["fp8", "bf16"], default="bf16")
     p.add_argument("--check-correctness", action="store_true")
     p.add_argument("--model-path", type=Path, default=None)
     core.add_timer_flags(p)
@@ -102,8 +109,9 @@ def run(argv=None) -> list[dict]:
 
     torch.manual_seed(a.seed)
     dev = torch.device("cuda")
-    inputs = make_inputs(a.tokens, a.dim, a.experts, a.topk, dev, a.seed)
-    weights = make_weights(a.dim, a.inter_dim, a.experts, dev, a.seed)
+    storage = torch.bfloat16 if a.input_dtype == "bf16" else fp8_dtype()
+    inputs = make_inputs(a.tokens, a.dim, a.experts, a.topk, dev, a.seed, storage)
+    weights = make_weights(a.dim, a.inter_dim, a.experts, dev, a.seed, storage)
     if a.backend == "torch":
         model = TorchMoE()
     else:

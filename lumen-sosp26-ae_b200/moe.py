@@ -152,6 +152,32 @@ def permute_rows(x: torch.Tensor, routes: SortedRoutes, out: torch.Tensor | None
     return out
 
 
+_fp8_luts: dict = {}
+
+
+def dequant_fp8_rows(q: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [T,H] = value(q[t,h]) * scale[t, h // 128] for fp8 q (any torch float8 dtype)."""
+    dev = _need_cuda(q, scale)
+    if q.element_size() != 1 or not q.dtype.is_floating_point:
+        raise ValueError(f"q must be a float8 tensor, got {q.dtype}")
+    T, H = q.shape
+    if H % 128 != 0 or tuple(scale.shape) != (T, H // 128) or scale.dtype != torch.float32:
+        raise ValueError("scale must be fp32 [T, H/128] and H a multiple of 128")
+    key = (dev.index, q.dtype)
+    lut = _fp8_luts.get(key)
+    if lut is None:  # the float value of each of the 256 codes of this fp8 flavour
+        lut = torch.arange(256, dtype=torch.uint8, device=dev).view(q.dtype).to(torch.float32)
+        lut = torch.nan_to_num(lut, nan=0.0, posinf=0.0, neginf=0.0).contiguous()
+        _fp8_luts[key] = lut
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    with _cabi.on_device(dev):
+        rc = _cabi.load().lumen_b200_moe_dequant_fp8(q.data_ptr(), scale.data_ptr(), lut.data_ptr(),
+                                                     out.data_ptr(), T, H, _stream(dev))
+    _cabi.check("lumen_b200_moe_dequant_fp8", rc)
+    return out
+
+
 _row_counts: dict = {}
 
 

@@ -63,3 +63,62 @@ def test_moe_host_validation(pkg):
     with pytest.raises(ValueError, match="no CPU path"):
         pkg.moe.route_topk(torch.zeros((2, 8)), 2)
     assert pkg.moe.max_padded_routes(4096, 2, 8) == 4096 * 2 + 8 * 32 - 2
+
+
+def test_null_arguments_are_refused_before_any_device_work(pkg):
+    """Every entry point validates its arguments first: with null pointers it returns
+    LUMEN_B200_EINVAL without touching a GPU (none exists where this test runs)."""
+    lib = pkg._cabi.load()
+    einval = pkg._cabi.EINVAL
+    assert lib.lumen_b200_gemm_bf16_nt(None, None, None, 4, 4, 8, 8, 8, 4, None, 0, None) == einval
+    assert lib.lumen_b200_gemm_bf16_nt_static(None, None, None, 4, 4, 8, 8, 8, 4, None) == einval
+    assert lib.lumen_b200_fa_fwd_bf16(None, None, None, None, 1, 8, 1, 1, 128, 0.1, 1, None) == einval
+    assert lib.lumen_b200_fa_fwd_varlen_bf16(None, None, None, None, None, 1, 8, 8, 1, 1, 128, 0.1, 1, None) == einval
+    assert lib.lumen_b200_moe_route_topk(None, None, None, 4, 8, 2, None) == einval
+    assert lib.lumen_b200_moe_router_logits(None, None, None, 4, 64, 8, None) == einval
+    assert lib.lumen_b200_moe_sort_routes(None, None, None, None, None, None, None, None, None, None, 0,
+                                          4, 8, 2, 32, None) == einval
+    assert lib.lumen_b200_moe_permute_rows(None, None, None, None, 4, 64, 8, None) == einval
+    assert lib.lumen_b200_moe_grouped_gemm(None, None, None, None, None, 8, 2, 64, 64, 0, 4, None) == einval
+    assert lib.lumen_b200_moe_combine(None, None, None, None, 4, 64, 2, None) == einval
+    assert lib.lumen_b200_moe_dequant_fp8(None, None, None, None, 4, 128, None) == einval
+    assert lib.lumen_b200_moe_ep_plan(None, 2, 8, 0, None, None, None, None, None, None) == einval
+    assert lib.lumen_b200_device_status(None) == einval
+    assert lib.lumen_b200_moe_sort_scratch_bytes(1000, 8, 2) == 2 * 8 * 4
+    assert lib.lumen_b200_gemm_static_scratch_limit() == 16 << 20
+    err = pkg._cabi.LumenB200Error("f", pkg._cabi.EWORKSPACE)
+    assert "EWORKSPACE" in str(err) and err.code == pkg._cabi.EWORKSPACE
+
+
+def test_harness_loader_follows_the_reference_entry_point_order(pkg, tmp_path):
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("harness_core_under_test", REPO / "lumen-sosp26-ae_b200" / "harness" / "core.py")
+    core = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(core)
+    src = tmp_path / "model.py"
+    src.write_text("class Model:\n    tag = 'model'\nclass ModelNew:\n    tag = 'new'\ndef kernel_function():\n    return 'fn'\n")
+    assert core.instantiate(core.import_by_path(src), device=torch.device("cpu")).tag == "new"
+    src.write_text("class Model:\n    tag = 'model'\ndef kernel_function():\n    return 'fn'\n")
+    assert core.instantiate(core.import_by_path(src), device=torch.device("cpu")).tag == "model"
+    src.write_text("def kernel_function():\n    return 'fn'\n")
+    assert core.instantiate(core.import_by_path(src), device=torch.device("cpu"))() == "fn"
+    src.write_text("x = 1\n")
+    with pytest.raises(RuntimeError, match="expected one of"):
+        core.instantiate(core.import_by_path(src), device=torch.device("cpu"))
+    assert core.default_model_path("gemm", "b200").exists()
+
+
+def test_bench_reference_arm_runs_without_a_gpu():
+    import json
+    import subprocess
+    import sys
+
+    out = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0"],
+                         capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    rec = json.loads(lines[0])
+    assert rec["impl"] == "reference" and rec["unit"] == "TFLOP/s" and rec["value"] > 0
+    assert rec["cpu_baseline"]["kind"] == "port" and rec["e2e"]["h2d_bytes_per_step"] == 0

@@ -46,3 +46,11 @@ def test_moe_cli_with_block_scales(cuda_pkg, capsys):
                                   "--topk", "2", "--check-correctness", *FAST])
     assert [r["tokens"] for r in recs] == [64, 700] and all(r["correctness"] for r in recs)
     assert cuda_pkg.device_status() == 0
+
+
+def test_moe_cli_fp8_storage(cuda_pkg, capsys):
+    """The reference harness' default storage: fp8 codes + block scales (compute stays bf16)."""
+    recs = load("bench_moe").run(["--tokens", "300", "--dim", "512", "--inter-dim", "256", "--experts", "8",
+                                  "--topk", "2", "--input-dtype", "fp8", "--check-correctness", *FAST])
+    assert recs[0]["input_dtype"] == "fp8" and recs[0]["correctness"]
+    assert cuda_pkg.device_status() == 0
