@@ -1,9 +1,14 @@
 """Expert-parallel MoE forward over the GPUs of one node.
 
 Tokens are sharded (T/G per rank: router, top-k and sort run locally), experts are
-sharded (E/G per rank, expert e lives on rank e // (E/G)).  The one exchange step each
-way is an all_to_all_single: per-expert counts first, then the expert-sorted activation
-rows (dispatch), and after the expert GEMMs the output rows back (combine).
+sharded (E/G per rank, expert e lives on rank e // (E/G)).  There is one exchange step each
+way: the expert-sorted activation rows go to the GPUs that own their experts (dispatch) and
+the expert outputs come back (return), before the local weighted combine.
+
+Two transports implement the exchange.  PeerExpertParallelMoE (the default choice on
+NVLink-connected GPUs) uses this library's own kernels, which store rows directly into the
+peers' buffers.  ExpertParallelMoE uses all_to_all_single collectives: per-expert counts
+first, one host read, then the rows with split sizes; the notes below describe it.
 
 Because the local sort is expert-major and experts are dealt out in contiguous runs, the
 compactly sorted rows are already grouped by destination rank: the gather kernel writes
