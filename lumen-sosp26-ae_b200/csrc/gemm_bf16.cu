@@ -3,6 +3,7 @@
 #include "gemm_bf16.cuh"
 #include "gemm_bf16_pair.cuh"
 #include <cstdlib>
+#include <string>
 #include "lumen_b200_internal.h"
 
 namespace b200 {
@@ -28,11 +29,11 @@ int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& ar
 }
 
 // dense GEMM on CTA pairs (clusters of 2); grid = 2 CTAs per co-resident cluster
+template <int STAGES, int BN>
 int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int units,
                      cudaStream_t st) {
-  constexpr int kStages = 6;
-  auto kern = gemm_bf16_pair_kernel<kStages>;
-  constexpr size_t smem = gemm_pair_smem_bytes<kStages>();
+  auto kern = gemm_bf16_pair_kernel<STAGES, BN>;
+  constexpr size_t smem = gemm_pair_smem_bytes<STAGES, BN>();
   static_assert(smem <= 227 * 1024, "stage ring does not fit shared memory");
   static bool configured[64] = {};
   static int max_clusters[64] = {};
@@ -59,6 +60,12 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
 
+// Width of the pair tile.  128-column tiles would cut the idle tail of the last wave in
+// half, but a 256 x 128 pair MMA runs at about two thirds of the 256 x 256 rate (measured:
+// 1035 against 1515 TFLOP/s on 8192 x 4096 x 4096), so the wide tile always wins; the narrow
+// instance stays selectable with LUMEN_B200_GEMM_TILE=pair128 for measurement.
+int pick_pair_tile_n(int, int, int) { return 256; }
+
 // Tile choice for the dense path: "pair" (256 x 256 per CTA pair) unless the environment
 // variable LUMEN_B200_GEMM_TILE says "single" (128 x 256 per CTA).
 bool use_pair_tiles() {
@@ -68,6 +75,18 @@ bool use_pair_tiles() {
     cached = (v && v[0] == 's') ? 0 : 1;
   }
   return cached == 1;
+}
+
+// LUMEN_B200_GEMM_TILE=pair128 / pair256 pins the pair tile width (0 = choose per shape)
+int forced_pair_tile_n() {
+  static int cached = -1;
+  if (cached < 0) {
+    const char* v = std::getenv("LUMEN_B200_GEMM_TILE");
+    cached = 0;
+    if (v && std::string(v) == "pair128") cached = 128;
+    if (v && std::string(v) == "pair256") cached = 256;
+  }
+  return cached;
 }
 
 inline int ceil_div_h(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
@@ -115,7 +134,7 @@ using namespace b200;
 static bool takes_streaming_path(int M, int N, int K, int sms) {
   if (M <= 128) return true;
   const long long pair_units =
-      static_cast<long long>((M + kPairTileM - 1) / kPairTileM) * ((N + kPairTileN - 1) / kPairTileN);
+      static_cast<long long>((M + kPairTileM - 1) / kPairTileM) * ((N + 255) / 256);
   const long long swap_tiles = static_cast<long long>((N + kBlockP - 1) / kBlockP) * ((M + 127) / 128);
   return pair_units * 5 < static_cast<long long>(sms / 2) * 2 && swap_tiles <= sms && K >= 512;
 }
@@ -155,10 +174,12 @@ extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, in
   const bool streaming = takes_streaming_path(M, N, K, sms);
   if (!streaming && use_pair_tiles()) {
     // CTA pairs: each CTA loads 128-row boxes of A and of B
+    const int bn = forced_pair_tile_n() ? forced_pair_tile_n() : pick_pair_tile_n(M, N, sms / 2);
     if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
-    if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, kBlockP) != 0) return LUMEN_B200_ECUDA;
-    const int units = ((M + kPairTileM - 1) / kPairTileM) * ((N + kPairTileN - 1) / kPairTileN);
-    return launch_gemm_pair(mp, mq, args, units, st);
+    if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, bn / 2) != 0) return LUMEN_B200_ECUDA;
+    const int units = ((M + kPairTileM - 1) / kPairTileM) * ((N + bn - 1) / bn);
+    return bn == 128 ? launch_gemm_pair<8, 128>(mp, mq, args, units, st)
+                     : launch_gemm_pair<6, 256>(mp, mq, args, units, st);
   }
   if (!streaming) {
     // P = A (128-row boxes), Q = B (256-row boxes)

@@ -18,8 +18,11 @@
 namespace b200 {
 
 constexpr int kPairTileM = 256;
-constexpr int kPairTileN = 256;
-constexpr int kPairStageBytes = 2 * kBlockP * kBlockK * 2;  // 16 KB of A + 16 KB of B per CTA
+// per CTA and stage: 128 rows of A (16 KB) + BN/2 rows of B
+template <int BN>
+__host__ __device__ constexpr int pair_stage_bytes() {
+  return kBlockP * kBlockK * 2 + (BN / 2) * kBlockK * 2;
+}
 
 template <int STAGES>
 struct PairSmemTail {
@@ -31,15 +34,16 @@ struct PairSmemTail {
   int abort_flag;
 };
 
-template <int STAGES>
+template <int STAGES, int BN>
 constexpr size_t gemm_pair_smem_bytes() {
-  return 1024 + size_t(STAGES) * kPairStageBytes + sizeof(PairSmemTail<STAGES>);
+  return 1024 + size_t(STAGES) * pair_stage_bytes<BN>() + sizeof(PairSmemTail<STAGES>);
 }
 
 struct PairUnit {
   int m0, n0;
 };
 
+template <int BN>
 __device__ __forceinline__ PairUnit pair_decode(int u, int tiles_m, int tiles_n) {
   // groups of 8 row tiles (2048 rows) sweep the column tiles together
   constexpr int kGroup = 8;
@@ -49,10 +53,12 @@ __device__ __forceinline__ PairUnit pair_decode(int u, int tiles_m, int tiles_n)
   const int gsz = min(kGroup, tiles_m - g * kGroup);
   const int nt = r / gsz;
   const int mt = g * kGroup + (r - nt * gsz);
-  return PairUnit{mt * kPairTileM, nt * kPairTileN};
+  return PairUnit{mt * kPairTileM, nt * BN};
 }
 
-template <int STAGES>
+// BN = 256 or 128 output columns per tile (the narrower tile halves the unit of work, which
+// matters when the tile count is a small non-multiple of the 74 CTA pairs).
+template <int STAGES, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                           const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
@@ -60,7 +66,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem_aligned = smem_raw + (smem_base - smem_u32(smem_raw));
-  Tail* tail = reinterpret_cast<Tail*>(smem_aligned + size_t(STAGES) * kPairStageBytes);
+  constexpr int kStageBytes = pair_stage_bytes<BN>();
+  constexpr int kTmemCols = 2 * BN;  // two accumulator buffers (256 or 512 columns)
+  Tail* tail = reinterpret_cast<Tail*>(smem_aligned + size_t(STAGES) * kStageBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -82,7 +90,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
   }
-  if (warp == 1) tmem_alloc(smem_u32(&tail->tmem_slot), 512);
+  if (warp == 1) tmem_alloc(smem_u32(&tail->tmem_slot), kTmemCols);
   tc_fence_before_sync();
   __syncthreads();
   cluster_sync_all();  // barriers of both CTAs are initialised before any remote arrival
@@ -90,7 +98,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 
   const uint32_t tmem_base = tail->tmem_slot;
   const int tiles_m = ceil_div(args.M, kPairTileM);
-  const int tiles_n = ceil_div(args.N, kPairTileN);
+  const int tiles_n = ceil_div(args.N, BN);
   const int total_units = tiles_m * tiles_n;
   const int k_blocks = ceil_div(args.K, kBlockK);
   const int pair_id = blockIdx.x >> 1;
@@ -103,17 +111,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int u = pair_id; u < total_units && ok; u += num_pairs) {
-        const PairUnit t = pair_decode(u, tiles_m, tiles_n);
+        const PairUnit t = pair_decode<BN>(u, tiles_m, tiles_n);
         const int a_row = t.m0 + int(rank) * kBlockP;
-        const int b_row = t.n0 + int(rank) * (kPairTileN / 2);
+        const int b_row = t.n0 + int(rank) * (BN / 2);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&tail->empty[stage]), phase ^ 1u, ctx, kWaitEmptyStage)) {
             ok = false;
             break;
           }
           const uint32_t leader_full = map_to_cta(smem_u32(&tail->full[stage]), 0);
-          if (rank == 0) mbar_arrive_expect_tx(smem_u32(&tail->full[stage]), 2 * kPairStageBytes);
-          const uint32_t sa = smem_base + stage * kPairStageBytes;
+          if (rank == 0) mbar_arrive_expect_tx(smem_u32(&tail->full[stage]), 2 * kStageBytes);
+          const uint32_t sa = smem_base + stage * kStageBytes;
           const uint32_t sb = sa + kBlockP * kBlockK * 2;
           tma_load_2d_pair(sa, &map_a, leader_full, kb * kBlockK, a_row);
           tma_load_2d_pair(sb, &map_b, leader_full, kb * kBlockK, b_row);
@@ -127,7 +135,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer (leader only) ======================
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kPairTileM, kPairTileN, 0, 0);
+      constexpr uint32_t idesc = make_idesc_bf16(kPairTileM, BN, 0, 0);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -140,14 +148,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + buf * kPairTileN;
+        const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&tail->full[stage]), phase, ctx, kWaitFullStage)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
-          const uint32_t sa = smem_base + stage * kPairStageBytes;
+          const uint32_t sa = smem_base + stage * kStageBytes;
           const uint32_t sb = sa + kBlockP * kBlockK * 2;
 #pragma unroll
           for (int k = 0; k < kBlockK / kUmmaK; ++k) {
@@ -172,7 +180,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     int it = 0;
     bool ok = true;
     for (int u = pair_id; u < total_units && ok; u += num_pairs, ++it) {
-      const PairUnit t = pair_decode(u, tiles_m, tiles_n);
+      const PairUnit t = pair_decode<BN>(u, tiles_m, tiles_n);
       const int buf = it & 1;
       const uint32_t buf_phase = (it >> 1) & 1;
       if (!mbar_wait(smem_u32(&tail->tmem_full[buf]), buf_phase, ctx, kWaitTmemFull)) {
@@ -181,13 +189,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
       __syncwarp();
       tc_fence_after_sync();
-      const uint32_t t_acc = tmem_base + (uint32_t(quad * 32) << 16) + buf * kPairTileN;
+      const uint32_t t_acc = tmem_base + (uint32_t(quad * 32) << 16) + buf * BN;
       const int row = t.m0 + int(rank) * kBlockP + p;
       const bool row_ok = row < args.M;
-      const int cols_valid = min(kPairTileN, args.N - t.n0);
+      const int cols_valid = min(BN, args.N - t.n0);
       __nv_bfloat16* orow = args.out + size_t(row) * args.ldo + t.n0;
 #pragma unroll 1
-      for (int c = 0; c < kPairTileN / 32; ++c) {
+      for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_acc + c * 32, v);
         tmem_ld_wait();
@@ -227,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
