@@ -1,8 +1,9 @@
 // BF16 contraction core for sm_100a:  D = P * Q^T with fp32 accumulation in TMEM.
 //
-// One persistent, warp-specialised kernel template serves the dense GEMM
-// (C = A * B^T), its small-M weight-streaming form, and the grouped (per-expert)
-// GEMMs of the MoE:
+// One persistent, warp-specialised kernel template, one CTA per tile.  It serves the
+// weight-streaming form of the dense GEMM C = A * B^T (few activation rows, split-K), the
+// grouped (per-expert) GEMMs of the MoE, and a 128 x 256 dense tiling; large dense
+// problems use the CTA-pair kernel of gemm_bf16_pair.cuh instead.
 //
 //   warp 0      TMA producer: global -> 128B-swizzled shared-memory ring (plain
 //               cp.async.bulk.tensor loads, one mbarrier per stage)
