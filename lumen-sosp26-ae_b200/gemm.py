@@ -12,17 +12,21 @@ import torch
 
 from . import _cabi
 
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_workspaces: dict[int, torch.Tensor] = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
-    """Per-device, per-stream split-K scratch, grown on demand (never shrunk)."""
+    """Split-K scratch of `device`, zero-filled when created and grown on demand (never
+    shrunk).  One buffer per device: GEMMs that take the split-K path must not overlap on
+    the GPU (launch them on one stream, or pass explicit workspaces through the C-ABI).
+    It is created by the first call that needs it, so make that call before capturing a
+    CUDA graph; replays then reuse it without a fill."""
     if nbytes == 0:
         return None
-    key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
+    key = device.index if device.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        ws = torch.zeros(max(nbytes, 32 << 20), dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws
 
