@@ -164,6 +164,14 @@ def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import torch
+
+    # torchrun exports OMP_NUM_THREADS=1 to its workers; the CPU arm uses every core it may
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    torch.set_num_threads(max(1, cores))
     times = []
     tf = 0.0
     threads = 1
