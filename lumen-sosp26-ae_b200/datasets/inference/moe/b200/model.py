@@ -131,26 +131,50 @@ class ModelNew(nn.Module):
                                       input_dtype="bf16" if input_q.dtype == torch.bfloat16 else "fp8")[0]()
 
 
-DIM = 4096
-INTER_DIM = 14336
-EXPERTS = 8
-TOPK = 2
-TOKENS = 4096
-SEED = 20260319
+# Defaults of get_inputs(): the Mixtral-like configuration.  An evaluator may override any
+# of them by setting a module-global EVAL_CONFIG dict (keys tokens, dim, inter_dim, experts,
+# topk, seed, device) before calling get_inputs(), the convention of the reference's
+# KernelBench-style MoE system (datasets/inference/moe/kernelbench/model.py:347-441).
+DEFAULTS = {"tokens": 4096, "dim": 4096, "inter_dim": 14336, "experts": 8, "topk": 2, "seed": 20260319,
+            "device": "cpu"}
+
+
+def _eval_config() -> dict:
+    cfg = dict(DEFAULTS)
+    raw = globals().get("EVAL_CONFIG", {})
+    if isinstance(raw, dict):
+        for key, default in DEFAULTS.items():
+            if key not in raw:
+                continue
+            try:
+                cfg[key] = type(default)(raw[key])
+            except (TypeError, ValueError):
+                pass
+    cfg["topk"] = max(1, min(cfg["topk"], cfg["experts"]))
+    return cfg
 
 
 def get_inputs():
-    """Mixtral-like stand-in inputs (x ~ N(0,1), weights ~ N(0,0.02), unit block scales)."""
-    g = torch.Generator().manual_seed(SEED)
-    x = torch.randn((TOKENS, DIM), generator=g, dtype=torch.float32).to(torch.bfloat16)
-    scores = torch.randn((TOKENS, EXPERTS), generator=g, dtype=torch.float32)
-    tv, ti = torch.topk(scores, k=TOPK, dim=-1, largest=True, sorted=True)
-    gw = torch.Generator().manual_seed(SEED + 17)
-    w1 = (torch.randn((EXPERTS, 2 * INTER_DIM, DIM), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
-    w2 = (torch.randn((EXPERTS, DIM, INTER_DIM), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    """Stand-in inputs (x ~ N(0,1), weights ~ N(0,0.02), unit block scales) in the argument
+    order of ModelNew.forward."""
+    c = _eval_config()
+    T, D, I, E, K = c["tokens"], c["dim"], c["inter_dim"], c["experts"], c["topk"]
+    g = torch.Generator().manual_seed(c["seed"])
+    x = torch.randn((T, D), generator=g, dtype=torch.float32).to(torch.bfloat16)
+    scores = torch.randn((T, E), generator=g, dtype=torch.float32)
+    tv, ti = torch.topk(scores, k=K, dim=-1, largest=True, sorted=True)
+    gw = torch.Generator().manual_seed(c["seed"] + 17)
+    w1 = torch.empty((E, 2 * I, D), dtype=torch.bfloat16)
+    w2 = torch.empty((E, D, I), dtype=torch.bfloat16)
+    for e in range(E):  # per expert: keeps the fp32 temporaries small
+        w1[e] = (torch.randn((2 * I, D), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    for e in range(E):
+        w2[e] = (torch.randn((D, I), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
     ones = lambda *s: torch.ones(s, dtype=torch.float32)  # noqa: E731
-    return [x, w1, w2, torch.softmax(tv, dim=-1), ti.to(torch.int32), ones(TOKENS, DIM // BLOCK),
-            ones(EXPERTS, (2 * INTER_DIM // BLOCK) * (DIM // BLOCK)), ones(EXPERTS, (DIM // BLOCK) * (INTER_DIM // BLOCK))]
+    out = [x, w1, w2, torch.softmax(tv, dim=-1), ti.to(torch.int32), ones(T, D // BLOCK),
+           ones(E, (2 * I // BLOCK) * (D // BLOCK)), ones(E, (D // BLOCK) * (I // BLOCK))]
+    dev = torch.device(c["device"])
+    return [t.to(dev) for t in out] if dev.type != "cpu" else out
 
 
 def get_init_inputs():

@@ -122,3 +122,36 @@ def test_bench_reference_arm_runs_without_a_gpu():
     rec = json.loads(lines[0])
     assert rec["impl"] == "reference" and rec["unit"] == "TFLOP/s" and rec["value"] > 0
     assert rec["cpu_baseline"]["kind"] == "port" and rec["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_model_files_follow_the_task_contract(pkg):
+    """get_inputs / get_init_inputs of every system (prompts/kernelbench/*.py contract) and the
+    MoE system's EVAL_CONFIG override."""
+    import importlib.util
+
+    def load(op):
+        path = REPO / "lumen-sosp26-ae_b200" / "datasets" / "inference" / op / "b200" / "model.py"
+        spec = importlib.util.spec_from_file_location(f"b200_model_{op}", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+
+    gemm = load("gemm")
+    assert gemm.get_init_inputs() == [] and hasattr(gemm, "ModelNew") and callable(gemm.kernel_function)
+    gemm.M, gemm.N, gemm.K = 8, 16, 32
+    a, b = gemm.get_inputs()
+    assert tuple(a.shape) == (8, 32) and tuple(b.shape) == (16, 32) and a.dtype == torch.bfloat16
+    attn = load("attention")
+    attn.batch_size, attn.sequence_length, attn.num_q_heads, attn.num_kv_heads = 1, 5, 4, 2
+    q, k, v = attn.get_inputs()
+    assert tuple(q.shape) == (1, 5, 4, 128) and tuple(k.shape) == (1, 5, 2, 128) and tuple(v.shape) == tuple(k.shape)
+    assert attn.ModelNew().causal is True and attn.ModelNew(causal=False).causal is False
+    moe = load("moe")
+    moe.EVAL_CONFIG = {"tokens": 8, "dim": 128, "inter_dim": 128, "experts": 4, "topk": 9, "seed": "x"}
+    xs = moe.get_inputs()
+    assert [tuple(t.shape) for t in xs] == [(8, 128), (4, 256, 128), (4, 128, 128), (8, 4), (8, 4), (8, 1),
+                                            (4, 2), (4, 1)]
+    assert xs[4].dtype == torch.int32 and float(xs[3].sum(dim=1).min()) > 0.999
+    with pytest.raises(ValueError, match="bf16 and fp8"):
+        moe.Model(variant="b200").build_cases(seq_len=8, shared_input=None, shared_weights={}, dim=128,
+                                              inter_dim=128, experts=4, topk=2, input_dtype="fp16")
