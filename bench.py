@@ -569,7 +569,7 @@ def run_ep_case(args) -> None:
         w2[e] = randn_bf16((H, I), 0.02)
     if args.transport == "peer":
         ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=Tl, hidden=H, inter=I, experts=E, topk=K, device=dev,
-                                              fused_return=args.fused_return)
+                                              fused_return=args.fused_return, sync=args.ep_sync)
     else:
         ops = pkg.moe_ep.CudaOps(dev, tokens_global=T, experts=E, topk=K)
         ep = pkg.moe_ep.ExpertParallelMoE(experts=E, topk=K, ops=ops)
@@ -624,6 +624,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--transport", choices=("peer", "nccl"), default="peer",
                     help="--case ep:*: how rows cross GPUs")
+    ap.add_argument("--ep-sync", choices=("signals", "nccl"), default="signals",
+                    help="--case ep:* --transport peer: how the GPUs synchronise")
     ap.add_argument("--fused-return", action="store_true",
                     help="--case ep:* --transport peer: the second expert GEMM's epilogue stores rows to their home GPU")
     ap.add_argument("--eager", action="store_true", help="--case: time eager launches instead of graph replays")

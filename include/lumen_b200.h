@@ -240,6 +240,24 @@ int lumen_b200_moe_ep_return(const void* y, const void* seg_start, const void* s
                              const void* const* peer_buffers, int G, int El, int H, int max_rows,
                              int home_capacity_rows, void* stream);
 
+/* Synchronisation of the G GPUs over peer memory, without a collective library.
+ * peer_signals: host array of G device pointers to each GPU's signal array (int32[64] in
+ * peer-accessible memory, zero before first use); epochs: this GPU's private int32[4],
+ * zero before first use; slot 0..3 selects an independent barrier.  The kernel announces
+ * this GPU's next epoch of the slot to every peer and waits (bounded: a wait that gives up
+ * is reported in the device status word) until every peer has announced it too.  All GPUs
+ * must issue the same sequence of calls per slot. */
+int lumen_b200_moe_ep_barrier(int rank, int G, const void* const* peer_signals, void* epochs,
+                              int slot, void* stream);
+
+/* All-gather of expert_counts[E] by peer stores followed by such a barrier: on completion
+ * row s of this GPU's count matrix (peer_count_matrices[rank], int32 [G,E]) holds GPU s's
+ * counts.  Input of lumen_b200_moe_ep_plan. */
+int lumen_b200_moe_ep_exchange_counts(const void* counts, int E, int rank, int G,
+                                      const void* const* peer_count_matrices,
+                                      const void* const* peer_signals, void* epochs, int slot,
+                                      void* stream);
+
 /* row_ptrs[g] (max_rows device pointers) = home address of grouped output row g: GPU
  * k % G, row seg_home_row[k] + (g - seg_start[k]) for the segment k that holds g; nullptr
  * past the last segment.  Input of lumen_b200_moe_grouped_gemm_to_rows. */

@@ -668,6 +668,68 @@ __global__ void __launch_bounds__(256)
   __threadfence_system();
 }
 
+// ---------------------------------------------------------------------------
+// Cross-GPU synchronisation over peer memory (no collective library on the data path).
+// Every GPU owns a signal array in symmetric memory: sig[slot * 16 + r] holds the last
+// epoch GPU r announced on that slot.  A barrier = bump this GPU's epoch of the slot, store
+// it into every peer's array (release, system scope), then wait until every peer's entry in
+// the local array has reached it (acquire).  Epochs only grow and every GPU runs the same
+// sequence of barriers, so ">=" is the completion test.  The wait is bounded like every
+// other wait in this library.
+// ---------------------------------------------------------------------------
+constexpr int kSigStride = 16;
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// called by one whole CTA; threads 0..G-1 do the signalling and the waiting
+__device__ void peer_barrier(const PeerPtrs& sigs, int* epochs, int slot, int rank, int G, int* status) {
+  __shared__ int s_epoch;
+  __threadfence_system();  // this GPU's earlier peer stores are visible before the signal
+  __syncthreads();
+  if (threadIdx.x == 0) s_epoch = ++epochs[slot];
+  __syncthreads();
+  const int epoch = s_epoch;
+  if (threadIdx.x < G) {
+    const int peer = threadIdx.x;
+    st_release_sys(static_cast<int*>(sigs.p[peer]) + slot * kSigStride + rank, epoch);
+    const int* mine = static_cast<const int*>(sigs.p[rank]) + slot * kSigStride + peer;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (ld_acquire_sys(mine) < epoch) {
+      if ((++spins & 0x3ffu) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicCAS(status, 0, (35 << 16) | (slot << 8) | peer);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
+// all-gather of the per-expert counts by peer stores, then a barrier: on return row s of
+// the local count matrix holds GPU s's counts
+__global__ void __launch_bounds__(1024)
+    moe_ep_exchange_counts_kernel(const int* __restrict__ counts, int E, int rank, int G, PeerPtrs matrices,
+                                  PeerPtrs sigs, int* epochs, int slot, int* status) {
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int c = counts[e];
+    for (int p = 0; p < G; ++p) static_cast<int*>(matrices.p[p])[rank * E + e] = c;
+  }
+  peer_barrier(sigs, epochs, slot, rank, G, status);
+}
+
+__global__ void __launch_bounds__(32)
+    moe_ep_barrier_kernel(PeerPtrs sigs, int* epochs, int slot, int rank, int G, int* status) {
+  peer_barrier(sigs, epochs, slot, rank, G, status);
+}
+
 // Address of every grouped output row on its way home: row g of segment k goes to GPU
 // k % G, row seg_home_row[k] + (g - seg_start[k]).  Rows past the last segment get nullptr.
 __global__ void __launch_bounds__(256)
@@ -714,6 +776,44 @@ extern "C" int lumen_b200_moe_ep_row_ptrs(const void* seg_start, const void* seg
   moe_ep_row_ptrs_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const int*>(seg_start), static_cast<const int*>(seg_home_row), peers, H, G, El * G,
       home_capacity_rows, max_rows, static_cast<__nv_bfloat16**>(row_ptrs), status);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+static bool fill_peers(PeerPtrs& peers, const void* const* ptrs, int G, uintptr_t align_mask) {
+  for (int g = 0; g < G; ++g) {
+    if (!ptrs[g] || (reinterpret_cast<uintptr_t>(ptrs[g]) & align_mask)) return false;
+    peers.p[g] = const_cast<void*>(ptrs[g]);
+  }
+  return true;
+}
+
+extern "C" int lumen_b200_moe_ep_exchange_counts(const void* counts, int E, int rank, int G,
+                                                  const void* const* peer_count_matrices,
+                                                  const void* const* peer_signals, void* epochs, int slot,
+                                                  void* stream) {
+  if (!counts || !peer_count_matrices || !peer_signals || !epochs) return LUMEN_B200_EINVAL;
+  if (G <= 0 || G > kMaxEpRanks || E <= 0 || E > kMaxExperts || rank < 0 || rank >= G || slot < 0 || slot >= 4)
+    return LUMEN_B200_EINVAL;
+  PeerPtrs mats{}, sigs{};
+  if (!fill_peers(mats, peer_count_matrices, G, 3) || !fill_peers(sigs, peer_signals, G, 3))
+    return LUMEN_B200_EINVAL;
+  int* status = device_status_word();
+  if (!status) return LUMEN_B200_ECUDA;
+  moe_ep_exchange_counts_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const int*>(counts), E, rank, G, mats, sigs, static_cast<int*>(epochs), slot, status);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_ep_barrier(int rank, int G, const void* const* peer_signals, void* epochs,
+                                          int slot, void* stream) {
+  if (!peer_signals || !epochs || G <= 0 || G > kMaxEpRanks || rank < 0 || rank >= G || slot < 0 || slot >= 4)
+    return LUMEN_B200_EINVAL;
+  PeerPtrs sigs{};
+  if (!fill_peers(sigs, peer_signals, G, 3)) return LUMEN_B200_EINVAL;
+  int* status = device_status_word();
+  if (!status) return LUMEN_B200_ECUDA;
+  moe_ep_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(sigs, static_cast<int*>(epochs), slot,
+                                                                          rank, G, status);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
 

@@ -261,15 +261,15 @@ class PeerExpertParallelMoE:
     buffer plus all_to_all.  The host reads nothing during a forward: every GPU derives the
     same offsets from the all-gathered G x E count matrix on the device.
 
-      route -> compact sort -> all_gather(counts) -> plan -> dispatch (peer stores)
-      -> barrier -> grouped GEMMs on the received rows -> return (peer stores)
+      route -> compact sort -> counts to every peer + barrier -> plan -> dispatch (peer
+      stores) -> barrier -> grouped GEMMs on the received rows -> return (peer stores)
       -> barrier -> weighted combine
 
     Buffers are sized for the worst case (every route of every GPU lands on one GPU).
     Construction is collective (symmetric-memory rendezvous)."""
 
     def __init__(self, *, tokens_local: int, hidden: int, inter: int, experts: int, topk: int,
-                 device: torch.device, group=None, fused_return: bool = False):
+                 device: torch.device, group=None, fused_return: bool = False, sync: str = "signals"):
         import ctypes
         import os
 
@@ -302,7 +302,23 @@ class PeerExpertParallelMoE:
         self.topk_ids = torch.empty((tokens_local, topk), dtype=i32, device=device)
         self.topk_weights = torch.empty((tokens_local, topk), dtype=torch.float32, device=device)
         self.logits = torch.empty((tokens_local, experts), dtype=torch.float32, device=device)
-        self.count_matrix = torch.zeros((self.G, experts), dtype=i32, device=device)
+        # sync = "signals": the GPUs meet through flags in each other's memory (this library's
+        # barrier kernel) and exchange their expert counts with peer stores, so a forward
+        # contains no collective-library call at all; sync = "nccl": all_gather + all_reduce
+        if sync not in ("signals", "nccl"):
+            raise ValueError("sync must be 'signals' or 'nccl'")
+        self.sync = sync
+        self.count_matrix = symm_mem.empty((self.G, experts), dtype=i32, device=device)
+        self.signals = symm_mem.empty((64,), dtype=i32, device=device)
+        self.count_matrix.zero_()
+        self.signals.zero_()
+        self._cm_hdl = symm_mem.rendezvous(self.count_matrix, self.group)
+        self._sig_hdl = symm_mem.rendezvous(self.signals, self.group)
+        self._cm_peers = ptr_array(*[int(p) for p in self._cm_hdl.buffer_ptrs])
+        self._sig_peers = ptr_array(*[int(p) for p in self._sig_hdl.buffer_ptrs])
+        self.epochs = torch.zeros((4,), dtype=i32, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)  # every GPU's flags are zero before anybody signals
         self.send_dst_start = torch.zeros((experts,), dtype=i32, device=device)
         self.local_offsets = torch.zeros((self.El + 1,), dtype=i32, device=device)
         self.local_counts = torch.zeros((self.El,), dtype=i32, device=device)
@@ -327,10 +343,16 @@ class PeerExpertParallelMoE:
         self._local = _Local()
         self._local.expert_offsets, self._local.expert_counts = self.local_offsets, self.local_counts
 
-    def _gpu_barrier(self):
+    def _gpu_barrier(self, slot: int):
         # stream-ordered rendezvous of all GPUs: nobody passes before everybody's earlier
         # kernels (the peer stores) have completed
-        dist.all_reduce(self._flag, group=self.group)
+        if self.sync == "nccl":
+            dist.all_reduce(self._flag, group=self.group)
+            return
+        with self._cabi.on_device(self.dev):
+            self._cabi.check("lumen_b200_moe_ep_barrier", self._cabi.load().lumen_b200_moe_ep_barrier(
+                self.rank, self.G, self._sig_peers, self.epochs.data_ptr(), slot,
+                torch.cuda.current_stream(self.dev).cuda_stream))
 
     def forward(self, x, w13_local, w2_local, *, logits=None, w_router=None, marks=None):
         moe, lib = self.moe, self._cabi.load()
@@ -349,7 +371,13 @@ class PeerExpertParallelMoE:
         r = moe.build_sorted_routes(topk_ids=self.topk_ids, topk_weights=self.topk_weights,
                                     experts=self.E, out=self.routes, scratch=self.scratch, group=1)
         mark("route+sort")
-        dist.all_gather_into_tensor(self.count_matrix.view(-1), r.expert_counts, group=self.group)
+        if self.sync == "nccl":
+            dist.all_gather_into_tensor(self.count_matrix.view(-1), r.expert_counts, group=self.group)
+        else:
+            with self._cabi.on_device(self.dev):
+                self._cabi.check("lumen_b200_moe_ep_exchange_counts", lib.lumen_b200_moe_ep_exchange_counts(
+                    r.expert_counts.data_ptr(), self.E, self.rank, self.G, self._cm_peers, self._sig_peers,
+                    self.epochs.data_ptr(), 0, stream))
         with self._cabi.on_device(self.dev):
             self._cabi.check("lumen_b200_moe_ep_plan", lib.lumen_b200_moe_ep_plan(
                 self.count_matrix.data_ptr(), self.G, self.E, self.rank, self.send_dst_start.data_ptr(),
@@ -360,7 +388,7 @@ class PeerExpertParallelMoE:
                 x.data_ptr(), r.sorted_token_ids.data_ptr(), r.sorted_expert_ids.data_ptr(),
                 r.expert_offsets.data_ptr(), self.send_dst_start.data_ptr(), r.num_valid_ids.data_ptr(),
                 self._recv_peers, self.G, self.T, self.H, self.E, self.T * self.k, self.capacity, stream))
-        self._gpu_barrier()
+        self._gpu_barrier(1)
         mark("dispatch (peer stores) + barrier")
         moe.grouped_gemm(self.recv, w13_local, self._local, gated=True, rows_hint=self.rows_hint, out=self.h)
         if self.fused_return:
@@ -378,7 +406,7 @@ class PeerExpertParallelMoE:
                 self._cabi.check("lumen_b200_moe_ep_return", lib.lumen_b200_moe_ep_return(
                     self.y.data_ptr(), self.seg_start.data_ptr(), self.seg_home_row.data_ptr(),
                     self._ret_peers, self.G, self.El, self.H, self.capacity, self.home_rows, stream))
-        self._gpu_barrier()
+        self._gpu_barrier(2)
         mark("return + barrier")
         out = moe.combine(self.ret, r, self.topk_weights, self.T, out=self.out)
         mark("combine")

@@ -94,15 +94,16 @@ def _worker(rank, world, port, result_dir):
             ids, w = moe_oracle.route_topk(logits, kk)
             want = moe_oracle.moe_reference(d["x"], d["w13"], d["w2"], ids, w)[t0:t1]
             outs = []
-            for fused in (False, True):  # return kernel, then GEMM epilogue storing to the home GPUs
+            # return kernel / GEMM epilogue storing to the home GPUs; signal barriers / NCCL
+            for fused, sync in ((False, "signals"), (True, "signals"), (False, "nccl")):
                 ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=tl, hidden=H, inter=I, experts=E, topk=kk,
-                                                      device=dev, fused_return=fused)
+                                                      device=dev, fused_return=fused, sync=sync)
                 for _ in range(2):  # twice: the second forward reuses every buffer
                     out = ep.forward(d["x"][t0:t1].to(dev), w13, w2, logits=logits[t0:t1].to(dev))
                     torch.cuda.synchronize()
                     torch.testing.assert_close(out.cpu().float(), want.float(), rtol=2e-2, atol=2e-2)
                 outs.append(out.cpu())
-            assert torch.equal(outs[0], outs[1])  # same arithmetic, different route home
+            assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])  # same arithmetic
             # the device plan equals its numpy specification
             counts = ep.count_matrix.cpu().numpy()
             ref = pkg.moe_ep.peer_plan(counts, rank)
