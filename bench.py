@@ -577,10 +577,24 @@ def run_ep_case(args) -> None:
         ep.forward(x, w13, w2, logits=logits)
     dist.barrier()
     torch.cuda.synchronize()
-    # eager launches: a CUDA graph holding the NCCL all_gather / all_reduce of the forward kept
-    # the communicator from shutting down at exit, so the case is not replayed as a graph
+    # Eager launches by default.  (A CUDA graph holding NCCL collectives kept the communicator
+    # from shutting down at exit.)  With the peer transport and signal barriers a forward
+    # contains no collective-library call, and --ep-graph replays it as one CUDA graph.
     run = lambda: ep.forward(x, w13, w2, logits=logits)  # noqa: E731
     timing = "eager launches"
+    graph = None
+    if args.ep_graph:
+        if args.transport != "peer" or args.ep_sync != "signals":
+            raise SystemExit("--ep-graph needs --transport peer --ep-sync signals")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run()
+        torch.cuda.synchronize()
+        dist.barrier()
+        run = graph.replay
+        timing = "CUDA graph replay"
+        run()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -591,6 +605,9 @@ def run_ep_case(args) -> None:
     t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    del run
+    graph = None  # release the graph before the process group goes away
+    torch.cuda.synchronize()
     # phase breakdown of one more forward on rank 0 (events between the phases)
     marks: list = []
     ep.forward(x, w13, w2, logits=logits, marks=marks)
@@ -626,6 +643,8 @@ def main() -> None:
                     help="--case ep:*: how rows cross GPUs")
     ap.add_argument("--ep-sync", choices=("signals", "nccl"), default="signals",
                     help="--case ep:* --transport peer: how the GPUs synchronise")
+    ap.add_argument("--ep-graph", action="store_true",
+                    help="--case ep:* with --transport peer --ep-sync signals: replay the forward as a CUDA graph")
     ap.add_argument("--fused-return", action="store_true",
                     help="--case ep:* --transport peer: the second expert GEMM's epilogue stores rows to their home GPU")
     ap.add_argument("--eager", action="store_true", help="--case: time eager launches instead of graph replays")

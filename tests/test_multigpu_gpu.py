@@ -115,6 +115,36 @@ def _worker(rank, world, port, result_dir):
             want_counts = np.stack([np.bincount(ids[r * tl:(r + 1) * tl].numpy().reshape(-1), minlength=E)
                                     for r in range(world)])
             assert np.array_equal(counts, want_counts)
+        # ---- the whole expert-parallel forward as one CUDA graph (no collective-library call
+        #      inside it), replayed with new tokens and new routing
+        T, H, I, E, kk = 128, 512, 256, 16, 4
+        tl, el = T // world, E // world
+        t0, t1 = rank * tl, (rank + 1) * tl
+        d = moe_oracle.moe_inputs(T, H, I, E, 77, with_router=False)
+        ep = pkg.moe_ep.PeerExpertParallelMoE(tokens_local=tl, hidden=H, inter=I, experts=E, topk=kk, device=dev)
+        w13, w2 = d["w13"][rank * el:(rank + 1) * el].to(dev), d["w2"][rank * el:(rank + 1) * el].to(dev)
+        x, lg = d["x"][t0:t1].to(dev), d["logits"][t0:t1].to(dev)
+        ep.forward(x, w13, w2, logits=lg)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = ep.forward(x, w13, w2, logits=lg)
+        torch.cuda.synchronize()
+        dist.barrier()
+        d2 = moe_oracle.moe_inputs(T, H, I, E, 78, with_router=False)
+        logits2 = d2["logits"].clone()
+        logits2[:, :2] += 4.0
+        x.copy_(d2["x"][t0:t1].to(dev))
+        lg.copy_(logits2[t0:t1].to(dev))
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        ids, w = moe_oracle.route_topk(logits2, kk)
+        want = moe_oracle.moe_reference(d2["x"], d["w13"], d["w2"], ids, w)[t0:t1]
+        torch.testing.assert_close(out.cpu().float(), want.float(), rtol=2e-2, atol=2e-2)
+        del graph
+        torch.cuda.synchronize()
+
         assert pkg.device_status() == 0
         dist.barrier()
         (Path(result_dir) / f"ok{rank}").write_text("ok")
