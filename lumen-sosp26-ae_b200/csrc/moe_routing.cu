@@ -289,6 +289,94 @@ __global__ void __launch_bounds__(kRouteChunk)
   }
 }
 
+// The same sort in one launch for up to 1024 routes (one CTA): histogram in shared memory,
+// padded scan over the experts, pad fill, stable rank, scatter.  Keeps the latency of the
+// small-batch (weight-streaming) MoE down: one launch instead of three.
+__global__ void __launch_bounds__(kRouteChunk)
+    moe_sort_one_cta_kernel(const int* __restrict__ ids, const float* __restrict__ weights,
+                            int* __restrict__ expert_offsets, int* __restrict__ expert_counts,
+                            int* __restrict__ sorted_token_ids, float* __restrict__ sorted_weights,
+                            int* __restrict__ sorted_expert_ids, int* __restrict__ num_valid_ids,
+                            int* __restrict__ route_pos, int T, int k, int E, int group) {
+  __shared__ int s_e[kRouteChunk];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_off[kMaxExperts];
+  __shared__ int s_warp[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int routes = T * k;
+
+  int e = -1;
+  if (tid < routes) {
+    e = ids[tid];
+    if (e < 0 || e >= E) e = -1;
+  }
+  s_e[tid] = e;
+  if (tid < E) s_cnt[tid] = 0;
+  const int max_padded = routes + E * group - k;
+  const int max_blocks = (max_padded + group - 1) / group;
+  const int sentinel = (k << 24) | T;
+  for (int i = tid; i < max_padded; i += blockDim.x) {
+    sorted_token_ids[i] = sentinel;
+    sorted_weights[i] = 0.f;
+  }
+  if (sorted_expert_ids)
+    for (int i = tid; i < max_blocks; i += blockDim.x) sorted_expert_ids[i] = -1;
+  __syncthreads();
+  if (e >= 0) atomicAdd(&s_cnt[e], 1);
+  __syncthreads();
+
+  // padded exclusive scan over the experts (E <= 1024 = one value per thread)
+  const int cnt = tid < E ? s_cnt[tid] : 0;
+  const int padded = (cnt + group - 1) / group * group;
+  int incl = padded;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += o;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = s_warp[lane];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w += o;
+    }
+    s_warp[lane] = w;
+  }
+  __syncthreads();
+  const int off = (warp == 0 ? 0 : s_warp[warp - 1]) + incl - padded;
+  if (tid < E) {
+    s_off[tid] = off;
+    expert_offsets[tid] = off;
+    expert_counts[tid] = cnt;
+    if (sorted_expert_ids)
+      for (int b = off / group; b < (off + padded) / group; ++b) sorted_expert_ids[b] = tid;
+  }
+  if (tid == 0) {
+    const int total = s_warp[31];
+    expert_offsets[E] = total;
+    num_valid_ids[0] = total;
+    num_valid_ids[1] = T;
+  }
+  __syncthreads();
+
+  // stable rank among the routes of the same expert, then scatter
+  const int warp_last = tid | 31;
+  int rank = 0;
+  for (int j = 0; j < warp_last; ++j) rank += (j < tid && s_e[j] == e) ? 1 : 0;
+  if (e >= 0) {
+    const int pos = s_off[e] + rank;
+    const int token = tid / k;
+    sorted_token_ids[pos] = ((tid - token * k) << 24) | token;
+    sorted_weights[pos] = weights[tid];
+    route_pos[tid] = pos;
+  } else if (tid < routes) {
+    route_pos[tid] = -1;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // gather rows into expert order: xs[pos][:] = x[token(pos)][:], pad rows = 0.
 // One CTA per sorted position; 16-byte accesses.
@@ -424,6 +512,15 @@ extern "C" int lumen_b200_moe_sort_routes(const void* topk_ids, const void* topk
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int routes = T * k;
   const int nchunks = (routes + kRouteChunk - 1) / kRouteChunk;
+  if (routes <= kRouteChunk) {
+    moe_sort_one_cta_kernel<<<1, kRouteChunk, 0, st>>>(
+        static_cast<const int*>(topk_ids), static_cast<const float*>(topk_weights),
+        static_cast<int*>(expert_offsets), static_cast<int*>(expert_counts),
+        static_cast<int*>(sorted_token_ids), static_cast<float*>(sorted_weights),
+        static_cast<int*>(sorted_expert_ids), static_cast<int*>(num_valid_ids), static_cast<int*>(route_pos),
+        T, k, E, route_group);
+    return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+  }
   int* hist = static_cast<int*>(scratch);
   moe_block_hist_kernel<<<nchunks, kRouteChunk, E * sizeof(int), st>>>(
       static_cast<const int*>(topk_ids), hist, routes, E);

@@ -89,6 +89,22 @@ def test_sorted_routes_random(cuda_pkg, T, E, k):
     check_routes(cuda_pkg, ids, w, E)
 
 
+@pytest.mark.parametrize("T,E,k", [(1, 256, 8), (100, 16, 4), (128, 8, 8), (2000, 64, 2)])
+def test_compact_sort_for_expert_parallel_dispatch(cuda_pkg, T, E, k):
+    """route_group = 1: experts back to back, one expert id per sorted row (both the one-CTA
+    and the three-kernel form)."""
+    g = torch.Generator().manual_seed(T + E)
+    ids, w = moe_oracle.route_topk(torch.randn((T, E), generator=g), k)
+    r = cuda_pkg.moe.build_sorted_routes(topk_ids=ids.to(DEV), topk_weights=w.to(DEV), experts=E, group=1)
+    torch.cuda.synchronize()
+    o = moe_oracle.build_sorted_routes(ids.numpy(), w.numpy(), E, group=1)
+    got = (r.sorted_token_ids, r.sorted_weights, r.sorted_expert_ids, r.num_valid_ids,
+           r.expert_offsets, r.expert_counts, r.route_pos)
+    for a, b in zip(got, o):
+        assert np.array_equal(a.cpu().numpy(), b)
+    assert int(r.num_valid_ids[0]) == T * k
+
+
 def test_sorted_routes_skewed_and_empty_experts(cuda_pkg):
     ids = torch.full((2100, 1), 3, dtype=torch.int32)  # every route on one expert, 3 chunks
     check_routes(cuda_pkg, ids, torch.ones((2100, 1)), 6)
