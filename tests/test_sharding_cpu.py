@@ -227,3 +227,54 @@ def test_expert_parallel_forward_over_gloo(tmp_path, world, skew):
     mp.spawn(_ep_worker, args=(world, _free_port(), T, H, I, E, k, skew, str(tmp_path)),
              nprocs=world, join=True)
     assert sorted(p.name for p in tmp_path.iterdir()) == [f"ok{r}" for r in range(world)]
+
+
+# ------------------------------------------------------------------ property checks
+def test_exchange_plans_hold_for_random_loads():
+    """Random count matrices (empty experts, empty senders, one hot expert): both plans are
+    permutations that group by expert with sources in rank order, and they agree."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    ep = _pkg().moe_ep
+
+    @settings(max_examples=60, deadline=None)
+    @given(st.integers(1, 4).flatmap(lambda g: st.tuples(
+        st.just(g), st.integers(1, 5).map(lambda el: el * g))).flatmap(lambda ge: st.tuples(
+            st.just(ge[0]), st.just(ge[1]),
+            st.lists(st.lists(st.integers(0, 7), min_size=ge[1], max_size=ge[1]), min_size=ge[0], max_size=ge[0]))))
+    def check(args):
+        G, E, rows = args
+        counts = np.array(rows, dtype=np.int64)
+        El = E // G
+        for rank in range(G):
+            mine = counts[:, rank * El:(rank + 1) * El]
+            rp = ep.regroup_plan(mine)
+            pp = ep.peer_plan(counts, rank)
+            total = int(mine.sum())
+            assert sorted(rp.gather.tolist()) == list(range(total))
+            assert np.array_equal(rp.gather[rp.scatter], np.arange(total))
+            assert np.array_equal(rp.expert_offsets, pp.local_offsets)
+            assert np.array_equal(rp.expert_counts, pp.local_counts)
+            assert int(pp.seg_start[-1]) == total and (np.diff(pp.seg_start) >= 0).all()
+            # segment (le, s) holds exactly the rows sender s has for local expert le
+            assert np.array_equal(np.diff(pp.seg_start).reshape(El, G), mine.T)
+            # a sender's rows of expert e start where the rows of its earlier experts end
+            assert np.array_equal(pp.seg_home_row.reshape(El, G),
+                                  (np.cumsum(counts, axis=1) - counts)[:, rank * El:(rank + 1) * El].T)
+        # every sender's destination ranges tile the owners' grouped buffers without overlap
+        for owner in range(G):
+            spans = []
+            for s in range(G):
+                p = ep.peer_plan(counts, s)
+                for e in range(owner * El, (owner + 1) * El):
+                    if counts[s, e]:
+                        spans.append((int(p.send_dst_start[e]), int(p.send_dst_start[e]) + int(counts[s, e])))
+            spans.sort()
+            pos = 0
+            for a, b in spans:
+                assert a == pos
+                pos = b
+            assert pos == int(counts[:, owner * El:(owner + 1) * El].sum())
+
+    check()
