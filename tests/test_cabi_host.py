@@ -4,7 +4,6 @@ from __future__ import annotations
 
 import ctypes
 import re
-from pathlib import Path
 
 import pytest
 import torch
