@@ -199,6 +199,23 @@ int lumen_b200_moe_grouped_gemm_to_rows(const void* acts, const void* weights,
 int lumen_b200_moe_combine(const void* y, const void* route_pos, const void* topk_weights,
                            void* out, int T, int H, int k, void* stream);
 
+/* The whole MoE forward in one call: top-k softmax of `logits` (skipped when the routing
+ * is given), stable sort of the routes, row gather, gated expert GEMM, second expert GEMM,
+ * weighted combine -- the entry points above launched in that order on `stream`, their
+ * intermediates carved out of `scratch` (at least lumen_b200_moe_forward_scratch_bytes(),
+ * no initial contents required).  x [T,H] bf16; w13 [E,2I,H] bf16, gate rows first; w2
+ * [E,H,I] bf16; out [T,H] bf16.  Give either logits [T,E] fp32 (topk_ids = topk_weights =
+ * NULL) or topk_ids [T,k] int32 + topk_weights [T,k] fp32 (logits = NULL), the routing the
+ * harness precomputes (scripts/benchmark/backend_moe.py:131-139).  H % 8 == 0, I % 8 == 0.
+ * Stands where the reference has one host call for the operator:
+ * fused_moe_fp8_blockscale_g1u1 (datasets/inference/moe/lumen/fused_moe.py:1439-1526) and
+ * run(8 tensors) of the native system (datasets/inference/moe/ksearch/main.cpp:113-245). */
+size_t lumen_b200_moe_forward_scratch_bytes(int T, int H, int I, int E, int k);
+int lumen_b200_moe_forward(const void* x, const void* w13, const void* w2, const void* logits,
+                           const void* topk_ids, const void* topk_weights, void* out,
+                           void* scratch, size_t scratch_bytes, int T, int H, int I, int E, int k,
+                           void* stream);
+
 /* out[T,H] (bf16) = lut[q[t,h]] * scale[t, h/128]: fp8 activations (one byte each) with
  * per-128-element fp32 scales to bf16.  lut = 256 floats, the value of every fp8 code
  * (covers e4m3fn and e4m3fnuz).  H % 128 == 0.  Stands in for the activation dequantisation

@@ -103,6 +103,12 @@ SIGNATURES = {
     ),
     "lumen_b200_moe_combine": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "lumen_b200_moe_forward_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "lumen_b200_moe_forward": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+         c_int, c_int, c_int, c_int, c_int, c_void_p],
+    ),
 }
 
 _lib = None

@@ -268,6 +268,48 @@ def combine(y: torch.Tensor, routes: SortedRoutes, topk_weights: torch.Tensor, t
     return out
 
 
+def moe_forward(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, *, topk: int,
+                logits: torch.Tensor | None = None, topk_ids: torch.Tensor | None = None,
+                topk_weights: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """The whole forward through the single C entry point lumen_b200_moe_forward: give either
+    `logits` [T,E] fp32 (the top-k softmax runs first) or precomputed `topk_ids` / `topk_weights`.
+    `scratch` (uint8, at least moe_forward_scratch_bytes(...)) holds every intermediate."""
+    dev = _need_cuda(x, w13, w2)
+    T, H = x.shape
+    E, two_i, H2 = w13.shape
+    inter = two_i // 2
+    if H2 != H or tuple(w2.shape) != (E, H, inter):
+        raise ValueError("w13 must be [E, 2I, H] and w2 [E, H, I].")
+    if (logits is None) == (topk_ids is None) or (topk_ids is None) != (topk_weights is None):
+        raise ValueError("give exactly one of logits or (topk_ids, topk_weights)")
+    if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (T, E)):
+        raise ValueError("logits must be float32 [T, E].")
+    if topk_ids is not None and (topk_ids.dtype != torch.int32 or topk_weights.dtype != torch.float32 or
+                                 tuple(topk_ids.shape) != (T, topk) or tuple(topk_weights.shape) != (T, topk)):
+        raise ValueError("topk_ids must be int32 [T, k] and topk_weights float32 [T, k].")
+    lib = _cabi.load()
+    need = moe_forward_scratch_bytes(T, H, inter, E, topk)
+    if scratch is None:
+        scratch = torch.empty((need,), dtype=torch.uint8, device=dev)
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    ptr = lambda t: 0 if t is None else t.data_ptr()  # noqa: E731
+    with _cabi.on_device(dev):
+        rc = lib.lumen_b200_moe_forward(
+            x.data_ptr(), w13.data_ptr(), w2.data_ptr(), ptr(logits), ptr(topk_ids), ptr(topk_weights),
+            out.data_ptr(), scratch.data_ptr(), scratch.numel(), T, H, inter, E, int(topk), _stream(dev))
+    _cabi.check("lumen_b200_moe_forward", rc)
+    return out
+
+
+def moe_forward_scratch_bytes(tokens: int, hidden: int, inter: int, experts: int, topk: int) -> int:
+    need = int(_cabi.load().lumen_b200_moe_forward_scratch_bytes(tokens, hidden, inter, experts, topk))
+    if need == 0:
+        raise ValueError("shape outside what lumen_b200_moe_forward covers")
+    return need
+
+
 class FusedMoE:
     """Pre-allocated buffers + the launch sequence of one MoE forward shape.
 

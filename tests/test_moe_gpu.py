@@ -167,3 +167,25 @@ def test_grouped_gemm_rows_are_independent(cuda_pkg):
     out2 = op2.forward(d["x"][perm].to(DEV), d["w13"].to(DEV), d["w2"].to(DEV), logits=d["logits"][perm].to(DEV))
     torch.cuda.synchronize()
     assert torch.equal(out2.cpu(), out[perm])
+
+
+@pytest.mark.parametrize("T,H,I,E,k", [(1, 512, 256, 16, 4), (200, 512, 384, 8, 2), (700, 384, 640, 4, 2)])
+def test_single_call_forward_equals_the_launch_sequence(cuda_pkg, T, H, I, E, k):
+    """lumen_b200_moe_forward (one C call, intermediates in one scratch buffer) launches the
+    same kernels as FusedMoE: identical bits, from logits and from precomputed routing, with
+    a scratch pointer that is not 256-byte aligned and holds garbage."""
+    d, op, out, ids, w = moe_case(cuda_pkg, T, H, I, E, k, 20260319 + T, False)
+    moe = cuda_pkg.moe
+    need = moe.moe_forward_scratch_bytes(T, H, I, E, k)
+    scratch = torch.full((need + 16,), 0xA5, dtype=torch.uint8, device=DEV)[16:]
+    x, w13, w2 = d["x"].to(DEV), d["w13"].to(DEV), d["w2"].to(DEV)
+    got = moe.moe_forward(x, w13, w2, topk=k, logits=d["logits"].to(DEV), scratch=scratch)
+    got_routed = moe.moe_forward(x, w13, w2, topk=k, topk_ids=ids.to(DEV), topk_weights=w.to(DEV))
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    assert torch.equal(got.cpu(), out)
+    assert torch.equal(got_routed.cpu(), out)
+    with pytest.raises(cuda_pkg._cabi.LumenB200Error):
+        moe.moe_forward(x, w13, w2, topk=k, logits=d["logits"].to(DEV), scratch=scratch[: need // 2])
+    with pytest.raises(ValueError):
+        moe.moe_forward(x, w13, w2, topk=k)
