@@ -83,6 +83,18 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     assert lib.lumen_b200_moe_dequant_fp8(None, None, None, None, 4, 128, None) == einval
     assert lib.lumen_b200_moe_ep_plan(None, 2, 8, 0, None, None, None, None, None, None) == einval
     assert lib.lumen_b200_device_status(None) == einval
+    assert lib.lumen_b200_moe_forward(None, None, None, None, None, None, None, None, 0, 4, 64, 64, 8, 2, None) == einval
+    # the single-call forward wants exactly one of logits / (topk_ids, topk_weights), and a sane shape
+    one = ctypes.c_void_p(256)  # never dereferenced: refused on the argument check
+    assert lib.lumen_b200_moe_forward(one, one, one, one, one, one, one, one, 1 << 30, 4, 64, 64, 8, 2, None) == einval
+    assert lib.lumen_b200_moe_forward(one, one, one, None, one, None, one, one, 1 << 30, 4, 64, 64, 8, 2, None) == einval
+    assert lib.lumen_b200_moe_forward(one, one, one, one, None, None, one, one, 1 << 30, 4, 64, 64, 8, 9, None) == einval
+    assert lib.lumen_b200_moe_forward(one, one, one, one, None, None, one, one, 1 << 30, 4, 60, 64, 8, 2, None) == einval
+    assert lib.lumen_b200_moe_forward(one, one, one, one, None, None, one, one, 64, 4, 64, 64, 8, 2, None) == pkg._cabi.EWORKSPACE
+    assert lib.lumen_b200_moe_forward_scratch_bytes(4, 60, 64, 8, 2) == 0
+    small, large = (lib.lumen_b200_moe_forward_scratch_bytes(t, 64, 64, 8, 2) for t in (4, 400))
+    rows = 4 * 2 + 8 * 32 - 2  # three [rows, 64] bf16 intermediates plus the route arrays
+    assert 3 * rows * 64 * 2 < small < large
     assert lib.lumen_b200_moe_sort_scratch_bytes(1000, 8, 2) == 2 * 8 * 4
     assert lib.lumen_b200_gemm_static_scratch_limit() == 16 << 20
     err = pkg._cabi.LumenB200Error("f", pkg._cabi.EWORKSPACE)
