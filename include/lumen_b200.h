@@ -50,6 +50,14 @@ int lumen_b200_device_status(int* status);
 /* Resets the device status word to 0 (synchronises). */
 int lumen_b200_clear_status(void);
 
+/* Enqueues on `stream` a copy of the device status word into *host_dst (page-locked host
+ * memory, so that the copy is asynchronous and can be captured in a CUDA graph).  Does not
+ * synchronise: the value is there once the work queued before it has run.  Lets a host loop
+ * notice a wait that gave up without stalling on lumen_b200_device_status() every step --
+ * the role the returned hipError_t plays for the reference's synchronous launch wrappers
+ * (datasets/inference/gemm/ksearch/kernel.h:7-17). */
+int lumen_b200_status_snapshot(int* host_dst, void* stream);
+
 /* ------------------------------------------------------------------ GEMM -- */
 
 /* C[M,N] = A[M,K] * B[N,K]^T, bf16 inputs, fp32 accumulation, bf16 output rounded
@@ -266,6 +274,15 @@ int lumen_b200_moe_ep_return(const void* y, const void* seg_start, const void* s
  * must issue the same sequence of calls per slot. */
 int lumen_b200_moe_ep_barrier(int rank, int G, const void* const* peer_signals, void* epochs,
                               int slot, void* stream);
+
+/* How long (nanoseconds) the two entry points around this comment wait for a peer before
+ * they give up, record (35 << 16 | slot << 8 | peer) in the device status word and return;
+ * 0 restores the default of 2 s.  A process-wide host setting read at launch.  It bounds the
+ * skew between the GPUs' launches: a peer that is later than this (first-call module load, a
+ * stalled host thread) makes the forward fail -- the expert-parallel kernels that follow skip
+ * their work while the status word is non-zero -- instead of hanging the GPU.  The reference
+ * has no multi-GPU path and no counterpart. */
+int lumen_b200_moe_ep_set_wait_limit_ns(unsigned long long limit_ns);
 
 /* All-gather of expert_counts[E] by peer stores followed by such a barrier: on completion
  * row s of this GPU's count matrix (peer_count_matrices[rank], int32 [G,E]) holds GPU s's

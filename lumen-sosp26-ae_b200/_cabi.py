@@ -34,6 +34,8 @@ SIGNATURES = {
     "lumen_b200_sm_count": (c_int, []),
     "lumen_b200_device_status": (c_int, [ctypes.POINTER(c_int)]),
     "lumen_b200_clear_status": (c_int, []),
+    "lumen_b200_status_snapshot": (c_int, [c_void_p, c_void_p]),
+    "lumen_b200_moe_ep_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
     "lumen_b200_gemm_bf16_nt": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t,

@@ -21,21 +21,35 @@
 // reference kernel (datasets/inference/attention/lumen/attn_06_inst_scheduling.py:694-716);
 // probabilities are exp2(s * scale * log2e - m * scale * log2e), rounded to bf16 for the
 // P V product as in the reference (:626,631), and summed in fp32.
+#include <cstdlib>
+
 #include "lumen_b200_internal.h"
 
 namespace b200 {
 
-constexpr int kFaThreads = 384;
+// 4 copy/MMA warps + two query tiles x SPLIT softmax warpgroups
+__host__ __device__ constexpr int fa_threads(int split) { return 128 + 256 * split; }
+// registers per thread after the setmaxnreg of each role; the launch allocation is
+// 65536 / threads rounded down to a multiple of 8 (168 for 384 threads, 96 for 640)
+__host__ __device__ constexpr int fa_regs_copy(int split) { return split == 1 ? 72 : 56; }
+__host__ __device__ constexpr int fa_regs_softmax(int split) { return split == 1 ? 216 : 104; }
+static_assert(128 * fa_regs_copy(1) + 256 * fa_regs_softmax(1) <= 384 * 168, "register file budget");
+static_assert(128 * fa_regs_copy(2) + 512 * fa_regs_softmax(2) <= 640 * 96, "register file budget");
 constexpr int kFaTile = 128;     // query rows per tile and keys per KV tile
 constexpr int kFaD = 128;        // head dimension
 constexpr int kFaHalfBytes = kFaTile * 64 * 2;   // one [128][64] bf16 swizzled panel
 constexpr int kFaTileBytes = 2 * kFaHalfBytes;   // one [128][128] tile = two panels
-constexpr int kFaRegsCopy = 72;      // registers per thread kept by the copy/MMA warpgroup
-constexpr int kFaRegsSoftmax = 216;  // registers per thread taken by the softmax warpgroups
-static_assert(128 * kFaRegsCopy + 256 * kFaRegsSoftmax <= 384 * 168, "register file budget");
 constexpr float kLazyRescaleLog2 = 8.0f;
-// evaluate every fourth exp2 with the FMA-pipe polynomial instead of the MUFU
-constexpr bool kExp2OnFmaPipe = false;
+
+// Compile-time choices of the softmax -> P V hand-off, template parameters of the kernel:
+//   FMA4     of every four exp2, this many run as a polynomial on the FMA pipe instead of the
+//            MUFU (the MUFU issues one warp instruction per 8 cycles, which bounds a softmax
+//            warp at 1024 cycles per 128 columns when every exp2 goes there)
+//   SPLIT    threads per query row in the softmax (1: one warpgroup per query tile, 384
+//            threads; 2: two warpgroups per tile, each thread owns 64 of the 128 keys, 640
+//            threads, so that two warps per scheduler work on a tile's softmax at once)
+//   PACKED   scale/subtract, the polynomial and the row sum use the two-wide fp32
+//            instructions (fma/add .f32x2), which halves their issue slots
 
 enum FaWaitCode {
   kFaWaitQ = 16,
@@ -44,6 +58,7 @@ enum FaWaitCode {
   kFaWaitS = 19,
   kFaWaitP = 20,
   kFaWaitO = 21,
+  kFaWaitRow = 22,
 };
 
 struct FaParams {
@@ -64,8 +79,11 @@ struct FaSmemTail {
   uint64_t s_ready[2];
   uint64_t p_ready[2];
   uint64_t o_done[2];
+  uint64_t row_xchg[2][4];  // [query tile][lane quadrant]: the warps that share those rows meet here
   uint32_t tmem_slot;
   int abort_flag;
+  float row_max[2 * 2 * kFaTile];  // [query tile][part][row] partial row maxima of one step
+  float row_sum[2 * 2 * kFaTile];  // the same for the final row sums
 };
 
 template <int SLOTS>
@@ -73,8 +91,49 @@ constexpr size_t fa_smem_bytes() {
   return 1024 + size_t(2 + SLOTS) * kFaTileBytes + sizeof(FaSmemTail<SLOTS>);
 }
 
-template <int SLOTS>
-__global__ void __launch_bounds__(kFaThreads, 1)
+// two fp32 values in one 64-bit register pair, for the .f32x2 instructions
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// exp2_fma (sm100_ptx.cuh) of two values at once on the two-wide FMA instructions
+__device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& p0, float& p1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t t = f2_add(x, magic);
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));
+  uint64_t p = f2_fma(f, f2_pack(0.0555041087f, 0.0555041087f), f2_pack(0.240226507f, 0.240226507f));
+  p = f2_fma(p, f, f2_pack(0.693147181f, 0.693147181f));
+  p = f2_fma(p, f, f2_pack(1.0f, 1.0f));
+  float t0, t1, q0, q1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(p, q0, q1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+template <int SLOTS, int SPLIT, int FMA4, bool PACKED>
+__global__ void __launch_bounds__(fa_threads(SPLIT), 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v, const FaParams prm) {
   using Tail = FaSmemTail<SLOTS>;
@@ -126,8 +185,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&tail->s_ready[t]), 1);
-      mbar_init(smem_u32(&tail->p_ready[t]), 128);
+      mbar_init(smem_u32(&tail->p_ready[t]), 4 * SPLIT);  // one elected lane per softmax warp
       mbar_init(smem_u32(&tail->o_done[t]), 1);
+      for (int q = 0; q < 4; ++q) mbar_init(smem_u32(&tail->row_xchg[t][q]), SPLIT);
     }
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -141,13 +201,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   tc_fence_after_sync();
   const uint32_t tmem_base = tail->tmem_slot;
 
-  // 384 threads x 168 registers at launch: the copy/MMA warpgroup keeps 56 per thread, the
-  // two softmax warpgroups take 224 (they hold a 128-wide score row per thread)
-  // (each role branch below starts with its own setmaxnreg so that the register bound of
-  // a branch is visible to the compiler)
+  // Registers: the copy/MMA warpgroup gives most of its launch allocation back, the softmax
+  // warpgroups take it (each role branch below starts with its own setmaxnreg so that the
+  // register bound of a branch is visible to the compiler).
+  constexpr int kRegsCopy = fa_regs_copy(SPLIT);
+  constexpr int kRegsSoftmax = fa_regs_softmax(SPLIT);
   if (warp == 0) {
     // ================================ TMA producer ======================================
-    reg_dealloc<kFaRegsCopy>();
+    reg_dealloc<kRegsCopy>();
     if (lane == 0) {
       const uint32_t qbar = smem_u32(&tail->q_full);
       const int active = (n_tiles[0] > 0 ? 1 : 0) + (n_tiles[1] > 0 ? 1 : 0);
@@ -177,7 +238,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
   } else if (warp == 1) {
     // ================================ MMA issuer ========================================
-    reg_dealloc<kFaRegsCopy>();
+    reg_dealloc<kRegsCopy>();
     if (lane == 0) {
       // S = Q K^T: both operands K-major (rows of 128 d-elements as two 64-wide panels)
       constexpr uint32_t idesc_qk = make_idesc_bf16(128, 128, 0, 0);
@@ -228,7 +289,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int j = 0; j < n_max && ok; ++j) {
         const int vseq = 2 * j + 1;
         const int kseq = 2 * j + 2;
-        bool v_ready = false, k_ready = false;
+        // V_j and K_{j+1} were requested steps ago (the ring is four tiles deep): confirm them
+        // now, while the softmax is still working, not between "P is ready" and the first P V MMA
+        ok = wait_full(vseq);
+        if (ok && j + 1 < n_max) ok = wait_full(kseq);
+        if (!ok) break;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= n_tiles[t]) continue;
           if (!mbar_wait(smem_u32(&tail->p_ready[t]), j & 1, ctx, kFaWaitP)) {
@@ -236,19 +301,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             break;
           }
           tc_fence_after_sync();
-          if (!v_ready) {
-            ok = wait_full(vseq);
-            if (!ok) break;
-            v_ready = true;
-          }
           issue_pv(t, slot_addr(vseq), j > 0);
           umma_commit(smem_u32(&tail->o_done[t]));
           if (j + 1 < n_tiles[t]) {
-            if (!k_ready) {
-              ok = wait_full(kseq);
-              if (!ok) break;
-              k_ready = true;
-            }
             issue_qk(t, slot_addr(kseq));
             umma_commit(smem_u32(&tail->s_ready[t]));
           }
@@ -259,24 +314,50 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
     }
   } else if (warp < 4) {
-    reg_dealloc<kFaRegsCopy>();
+    reg_dealloc<kRegsCopy>();
   } else {
     // ================================ softmax + epilogue ================================
-    reg_alloc<kFaRegsSoftmax>();
-    const int t = (warp - 4) >> 2;          // query tile of this warpgroup
+    // SPLIT threads share a row: thread `part` owns the kCols consecutive keys / output
+    // columns [part * kCols, +kCols) of it.  The SPLIT warps of one (tile, lane quadrant)
+    // exchange their partial row maxima and sums through shared memory.
+    reg_alloc<kRegsSoftmax>();
+    constexpr int kCols = kFaTile / SPLIT;
+    constexpr int kChunks = kCols / 32;
+    const int sw = warp - 4;
+    const int t = sw / (4 * SPLIT);         // query tile of this warp
+    const int part = (sw >> 2) % SPLIT;     // which columns of the row
     const int quad = warp & 3;              // TMEM lane quadrant
     const int r = quad * 32 + lane;         // row of the tile
     const int q = q0 + t * kFaTile + r;     // query position
     const int n = n_tiles[t];
     const uint32_t lane_sel = uint32_t(quad * 32) << 16;
-    const uint32_t s_tmem = tmem_base + lane_sel + t * 128;
-    const uint32_t o_tmem = tmem_base + lane_sel + 256 + t * 128;
+    const uint32_t s_tmem = tmem_base + lane_sel + t * 128 + part * kCols;        // my S columns
+    const uint32_t p_tmem = tmem_base + lane_sel + t * 128 + part * (kCols / 2);  // my packed P columns
+    const uint32_t o_tmem = tmem_base + lane_sel + 256 + t * 128 + part * kCols;  // my O columns
     const float sl2 = prm.scale_log2;
     // last key this row may see
     const int kv_lim = prm.causal ? min(q, seq_len - 1) : seq_len - 1;
+    const uint32_t xbar = smem_u32(&tail->row_xchg[t][quad]);
+    uint32_t xphase = 0;
+    // value of the row's other part(s): publish mine, meet, read theirs
+    auto row_exchange = [&](float* slots, float mine, auto combine, bool& ok) {
+      if constexpr (SPLIT == 1) {
+        return mine;
+      } else {
+        slots[(t * SPLIT + part) * kFaTile + r] = mine;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+        if (!mbar_wait(xbar, xphase, ctx, kFaWaitRow)) ok = false;
+        xphase ^= 1u;
+        float v = mine;
+#pragma unroll
+        for (int o = 1; o < SPLIT; ++o) v = combine(v, slots[(t * SPLIT + ((part + o) % SPLIT)) * kFaTile + r]);
+        return v;
+      }
+    };
 
     float m = -INFINITY;  // running maximum (raw score units)
-    float l = 0.f;        // running sum of probabilities
+    float l = 0.f;        // running sum of this thread's probabilities
     bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
       if (!mbar_wait(smem_u32(&tail->s_ready[t]), j & 1, ctx, kFaWaitS)) {
@@ -285,33 +366,37 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
       __syncwarp();
       tc_fence_after_sync();
-      uint32_t sv[4][32];
+      uint32_t sv[kChunks][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_tmem + c * 32, sv[c]);
+      for (int c = 0; c < kChunks; ++c) tmem_ld_32x32b_x32(s_tmem + c * 32, sv[c]);
       tmem_ld_wait();
 
-      const int cmax = kv_lim - j * kFaTile;  // columns [0, cmax] are visible
-      if (cmax < kFaTile - 1) {
+      const int cmax = kv_lim - j * kFaTile - part * kCols;  // my columns [0, cmax] are visible
+      if (cmax < kCols - 1) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < kChunks; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i > cmax) sv[c][i] = __float_as_uint(-INFINITY);
       }
-      // row maximum: four independent chains of three-input max
-      float mxc[4];
+      // row maximum: independent chains of three-input max
+      float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kChunks; ++c) {
         float a = max3(__uint_as_float(sv[c][0]), __uint_as_float(sv[c][1]), __uint_as_float(sv[c][2]));
 #pragma unroll
         for (int i = 3; i + 1 < 32; i += 2)
           a = max3(a, __uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1]));
-        mxc[c] = fmaxf(a, __uint_as_float(sv[c][31]));
+        mx = fmaxf(mx, fmaxf(a, __uint_as_float(sv[c][31])));
       }
-      const float mx = fmaxf(fmaxf(mxc[0], mxc[1]), fmaxf(mxc[2], mxc[3]));
+      // After this meeting every part has its S columns in registers, so the packed P of a
+      // later part may overwrite the S columns of an earlier one.
+      mx = row_exchange(tail->row_max, mx, [](float a, float b2) { return fmaxf(a, b2); }, ok);
+      if (!ok) break;
 
       // lazy rescale: raise m only when the tile maximum is far above it (warp-uniform,
-      // because the O update below is a warp-collective TMEM access)
+      // because the O update below is a warp-collective TMEM access; the parts of a row
+      // see the same maximum, so their warps decide alike)
       const bool need = (mx - m) * sl2 > kLazyRescaleLog2;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = fmaxf(m, mx);
@@ -326,7 +411,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           __syncwarp();
           tc_fence_after_sync();
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t ov[32];
             tmem_ld_32x32b_x32(o_tmem + c * 32, ov);
             tmem_ld_wait();
@@ -339,51 +424,78 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
 
       const float neg_m = -m * sl2;
-      // probabilities; four independent partial sums.  (kExp2OnFmaPipe moves every fourth
-      // exp2 from the MUFU to the FMA pipe.)
+      // probabilities p = 2^(s * sl2 - m * sl2); four independent partial sums
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint64_t sum2[2] = {0ull, 0ull};  // PACKED: (sum of p0, sum of p1), (sum of p2, sum of p3)
+      const uint64_t sl2_2 = f2_pack(sl2, sl2);
+      const uint64_t neg_m2 = f2_pack(neg_m, neg_m);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
+      for (int c = 0; c < kChunks; ++c) {
+        // 32 keys -> 16 packed columns, stored to TMEM as soon as they are complete
+        uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float x0 = fmaf(__uint_as_float(sv[half * 2 + c][i + 0]), sl2, neg_m);
-            const float x1 = fmaf(__uint_as_float(sv[half * 2 + c][i + 1]), sl2, neg_m);
-            const float x2 = fmaf(__uint_as_float(sv[half * 2 + c][i + 2]), sl2, neg_m);
-            const float x3 = fmaf(__uint_as_float(sv[half * 2 + c][i + 3]), sl2, neg_m);
-            const float p0 = fast_exp2(x0);
-            const float p1 = fast_exp2(x1);
-            const float p2 = fast_exp2(x2);
-            const float p3 = kExp2OnFmaPipe ? exp2_fma(x3) : fast_exp2(x3);
+        for (int i = 0; i < 32; i += 4) {
+          const uint32_t* s4 = &sv[c][i];
+          float x0, x1, x2, x3;
+          if constexpr (PACKED) {
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(s4[0]), __uint_as_float(s4[1])), sl2_2, neg_m2), x0, x1);
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(s4[2]), __uint_as_float(s4[3])), sl2_2, neg_m2), x2, x3);
+          } else {
+            x0 = fmaf(__uint_as_float(s4[0]), sl2, neg_m);
+            x1 = fmaf(__uint_as_float(s4[1]), sl2, neg_m);
+            x2 = fmaf(__uint_as_float(s4[2]), sl2, neg_m);
+            x3 = fmaf(__uint_as_float(s4[3]), sl2, neg_m);
+          }
+          float p0, p1, p2, p3;
+          p0 = FMA4 >= 4 ? exp2_fma(x0) : fast_exp2(x0);
+          p1 = FMA4 >= 3 ? exp2_fma(x1) : fast_exp2(x1);
+          if constexpr (PACKED && FMA4 == 2) {
+            exp2_fma_pair(x2, x3, p2, p3);
+          } else {
+            p2 = FMA4 >= 2 ? exp2_fma(x2) : fast_exp2(x2);
+            p3 = FMA4 >= 1 ? exp2_fma(x3) : fast_exp2(x3);
+          }
+          if constexpr (PACKED) {
+            sum2[0] = f2_add(sum2[0], f2_pack(p0, p1));
+            sum2[1] = f2_add(sum2[1], f2_pack(p2, p3));
+          } else {
             sum4[0] += p0;
             sum4[1] += p1;
             sum4[2] += p2;
             sum4[3] += p3;
-            pk[c * 16 + i / 2] = pack_bf16x2(p0, p1);
-            pk[c * 16 + i / 2 + 1] = pack_bf16x2(p2, p3);
           }
+          pk[i / 2] = pack_bf16x2(p0, p1);
+          pk[i / 2 + 1] = pack_bf16x2(p2, p3);
         }
-        tmem_st_32x32b_x32(s_tmem + half * 32, pk);
+        tmem_st_32x32b_x16(p_tmem + c * 16, pk);
       }
-      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-      l += sum;
+      if constexpr (PACKED) {
+        f2_unpack(sum2[0], sum4[0], sum4[1]);
+        f2_unpack(sum2[1], sum4[2], sum4[3]);
+      }
+      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      // my part of P is complete in TMEM: one elected lane per warp tells the MMA thread
       tmem_st_wait();
       tc_fence_before_sync();
-      mbar_arrive(smem_u32(&tail->p_ready[t]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tail->p_ready[t]));
     }
 
     // ---- epilogue: O / l -> bf16 -> global -------------------------------------------
+    if (n > 0) {
+      bool met = true;  // every part takes this meeting, also after a wait gave up
+      l = row_exchange(tail->row_sum, l, [](float a, float b2) { return a + b2; }, met);
+      ok = ok && met;
+    }
     if (ok && n > 0) {
       if (mbar_wait(smem_u32(&tail->o_done[t]), (n - 1) & 1, ctx, kFaWaitO)) {
         __syncwarp();
         tc_fence_after_sync();
         const float inv_l = 1.0f / l;
         __nv_bfloat16* orow =
-            prm.O + ((size_t(row_base) + q) * prm.Hq + hq) * kFaD;
+            prm.O + ((size_t(row_base) + q) * prm.Hq + hq) * kFaD + part * kCols;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < kChunks; ++c) {
           uint32_t ov[32];
           tmem_ld_32x32b_x32(o_tmem + c * 32, ov);
           tmem_ld_wait();
@@ -423,6 +535,37 @@ using namespace b200;
 
 namespace {
 
+template <int SPLIT, int FMA4, bool PACKED>
+int launch_fa_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FaParams& prm,
+                      long long grid, cudaStream_t st) {
+  constexpr int kSlots = 4;
+  auto kern = fa_fwd_kernel<kSlots, SPLIT, FMA4, PACKED>;
+  constexpr size_t smem = fa_smem_bytes<kSlots>();
+  static_assert(smem <= 227 * 1024, "K/V ring does not fit shared memory");
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LUMEN_B200_ECUDA;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+    configured[dev] = true;
+  }
+  kern<<<static_cast<unsigned>(grid), fa_threads(SPLIT), smem, st>>>(mq, mk, mv, prm);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+// Which instantiation runs.  LUMEN_B200_FA_VARIANT (a digit, read once) selects one of the
+// measured alternatives; unset = the default.
+int fa_variant() {
+  static int cached = -1;
+  if (cached < 0) {
+    const char* v = std::getenv("LUMEN_B200_FA_VARIANT");
+    cached = (v && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 0;
+  }
+  return cached;
+}
+
 // rows = packed tokens; S_max = longest sequence (sizes the grid)
 int launch_fa(const void* Q, const void* K, const void* V, void* O, const int* seq_ptr, int B, int S_uniform,
               long long rows, int S_max, int Hq, int Hkv, float scale, int causal, cudaStream_t st) {
@@ -451,22 +594,24 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, const int* s
   prm.q_blocks = (S_max + 2 * kFaTile - 1) / (2 * kFaTile);
   prm.status = status;
 
-  constexpr int kSlots = 4;
-  auto kern = fa_fwd_kernel<kSlots>;
-  constexpr size_t smem = fa_smem_bytes<kSlots>();
-  static bool configured[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LUMEN_B200_ECUDA;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return LUMEN_B200_ECUDA;
-    configured[dev] = true;
-  }
   const long long grid = static_cast<long long>(prm.q_blocks) * B * Hq;
   if (grid <= 0 || grid > 0x7fffffffLL) return LUMEN_B200_EUNSUPPORTED;
-  kern<<<static_cast<unsigned>(grid), kFaThreads, smem, st>>>(mq, mk, mv, prm);
-  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+  switch (fa_variant()) {
+    case 0:
+      return launch_fa_variant<1, 0, false>(mq, mk, mv, prm, grid, st);
+    case 1:
+      return launch_fa_variant<2, 0, false>(mq, mk, mv, prm, grid, st);
+    case 2:
+      return launch_fa_variant<2, 1, false>(mq, mk, mv, prm, grid, st);
+    case 3:
+      return launch_fa_variant<2, 1, true>(mq, mk, mv, prm, grid, st);
+    case 4:
+      return launch_fa_variant<2, 2, true>(mq, mk, mv, prm, grid, st);
+    case 5:
+      return launch_fa_variant<2, 0, true>(mq, mk, mv, prm, grid, st);
+    default:
+      return launch_fa_variant<2, 2, false>(mq, mk, mv, prm, grid, st);
+  }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }

@@ -641,7 +641,11 @@ struct PeerPtrs {
 __global__ void __launch_bounds__(1024)
     moe_ep_plan_kernel(const int* __restrict__ counts, int G, int E, int rank, int* __restrict__ send_dst_start,
                        int* __restrict__ local_offsets, int* __restrict__ local_counts,
-                       int* __restrict__ seg_start, int* __restrict__ seg_home_row) {
+                       int* __restrict__ seg_start, int* __restrict__ seg_home_row,
+                       const int* __restrict__ status) {
+  // after a wait that gave up (a barrier that ran out) the count matrix may be incomplete:
+  // keep the previous plan, whose offsets are in bounds, and let the host see the status
+  if (*status != 0) return;
   __shared__ int s_prefix[kMaxExperts + 1];  // exclusive prefix over experts of the column totals
   __shared__ int s_warp[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -718,6 +722,7 @@ __global__ void __launch_bounds__(256)
                            const int* __restrict__ row_expert, const int* __restrict__ expert_offsets,
                            const int* __restrict__ send_dst_start, const int* __restrict__ num_valid_ids,
                            PeerPtrs peers, int T, int H, int El, int capacity_rows, int* status) {
+  if (*status != 0) return;  // an earlier wait gave up: move nothing across GPUs
   const int total = num_valid_ids[0];
   const int chunks = H / 8;
   for (int pos = blockIdx.x; pos < total; pos += gridDim.x) {
@@ -742,6 +747,7 @@ __global__ void __launch_bounds__(256)
     moe_ep_return_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ seg_start,
                          const int* __restrict__ seg_home_row, PeerPtrs peers, int H, int G, int nseg,
                          int home_capacity_rows, int* status) {
+  if (*status != 0) return;  // an earlier wait gave up: move nothing across GPUs
   const int total = seg_start[nseg];
   const int chunks = H / 8;
   for (int g = blockIdx.x; g < total; g += gridDim.x) {
@@ -786,7 +792,8 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 }
 
 // called by one whole CTA; threads 0..G-1 do the signalling and the waiting
-__device__ void peer_barrier(const PeerPtrs& sigs, int* epochs, int slot, int rank, int G, int* status) {
+__device__ void peer_barrier(const PeerPtrs& sigs, int* epochs, int slot, int rank, int G, int* status,
+                             uint64_t limit_ns) {
   __shared__ int s_epoch;
   __threadfence_system();  // this GPU's earlier peer stores are visible before the signal
   __syncthreads();
@@ -800,7 +807,7 @@ __device__ void peer_barrier(const PeerPtrs& sigs, int* epochs, int slot, int ra
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
     while (ld_acquire_sys(mine) < epoch) {
-      if ((++spins & 0x3ffu) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+      if ((++spins & 0x3ffu) == 0u && globaltimer_ns() - t0 > limit_ns) {
         atomicCAS(status, 0, (35 << 16) | (slot << 8) | peer);
         break;
       }
@@ -814,18 +821,22 @@ __device__ void peer_barrier(const PeerPtrs& sigs, int* epochs, int slot, int ra
 // the local count matrix holds GPU s's counts
 __global__ void __launch_bounds__(1024)
     moe_ep_exchange_counts_kernel(const int* __restrict__ counts, int E, int rank, int G, PeerPtrs matrices,
-                                  PeerPtrs sigs, int* epochs, int slot, int* status) {
+                                  PeerPtrs sigs, int* epochs, int slot, int* status, uint64_t limit_ns) {
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int c = counts[e];
     for (int p = 0; p < G; ++p) static_cast<int*>(matrices.p[p])[rank * E + e] = c;
   }
-  peer_barrier(sigs, epochs, slot, rank, G, status);
+  peer_barrier(sigs, epochs, slot, rank, G, status, limit_ns);
 }
 
 __global__ void __launch_bounds__(32)
-    moe_ep_barrier_kernel(PeerPtrs sigs, int* epochs, int slot, int rank, int G, int* status) {
-  peer_barrier(sigs, epochs, slot, rank, G, status);
+    moe_ep_barrier_kernel(PeerPtrs sigs, int* epochs, int slot, int rank, int G, int* status,
+                          uint64_t limit_ns) {
+  peer_barrier(sigs, epochs, slot, rank, G, status, limit_ns);
 }
+
+// How long a GPU waits for its peers in the barriers above; host-side setting of this process.
+static uint64_t g_ep_wait_limit_ns = kWaitLimitNs;
 
 // Address of every grouped output row on its way home: row g of segment k goes to GPU
 // k % G, row seg_home_row[k] + (g - seg_start[k]).  Rows past the last segment get nullptr.
@@ -897,8 +908,14 @@ extern "C" int lumen_b200_moe_ep_exchange_counts(const void* counts, int E, int 
   int* status = device_status_word();
   if (!status) return LUMEN_B200_ECUDA;
   moe_ep_exchange_counts_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const int*>(counts), E, rank, G, mats, sigs, static_cast<int*>(epochs), slot, status);
+      static_cast<const int*>(counts), E, rank, G, mats, sigs, static_cast<int*>(epochs), slot, status,
+      g_ep_wait_limit_ns);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+extern "C" int lumen_b200_moe_ep_set_wait_limit_ns(unsigned long long limit_ns) {
+  g_ep_wait_limit_ns = limit_ns ? static_cast<uint64_t>(limit_ns) : kWaitLimitNs;
+  return LUMEN_B200_OK;
 }
 
 extern "C" int lumen_b200_moe_ep_barrier(int rank, int G, const void* const* peer_signals, void* epochs,
@@ -910,7 +927,7 @@ extern "C" int lumen_b200_moe_ep_barrier(int rank, int G, const void* const* pee
   int* status = device_status_word();
   if (!status) return LUMEN_B200_ECUDA;
   moe_ep_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(sigs, static_cast<int*>(epochs), slot,
-                                                                          rank, G, status);
+                                                                          rank, G, status, g_ep_wait_limit_ns);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
 
@@ -921,10 +938,12 @@ extern "C" int lumen_b200_moe_ep_plan(const void* counts, int G, int E, int rank
     return LUMEN_B200_EINVAL;
   if (G <= 0 || G > kMaxEpRanks || E <= 0 || E > kMaxExperts || E % G != 0 || rank < 0 || rank >= G)
     return LUMEN_B200_EINVAL;
+  const int* status = device_status_word();
+  if (!status) return LUMEN_B200_ECUDA;
   moe_ep_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const int*>(counts), G, E, rank, static_cast<int*>(send_dst_start),
       static_cast<int*>(local_offsets), static_cast<int*>(local_counts), static_cast<int*>(seg_start),
-      static_cast<int*>(seg_home_row));
+      static_cast<int*>(seg_home_row), status);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
 

@@ -113,3 +113,13 @@ extern "C" int lumen_b200_clear_status(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return LUMEN_B200_ECUDA;
   return cudaMemset(p, 0, sizeof(int)) == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
 }
+
+extern "C" int lumen_b200_status_snapshot(int* host_dst, void* stream) {
+  if (!host_dst) return LUMEN_B200_EINVAL;
+  int* p = b200::device_status_word();
+  if (!p) return LUMEN_B200_ECUDA;
+  return cudaMemcpyAsync(host_dst, p, sizeof(int), cudaMemcpyDeviceToHost,
+                         static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? LUMEN_B200_OK
+             : LUMEN_B200_ECUDA;
+}

@@ -51,22 +51,51 @@ _moe = _pkg.moe
 BLOCK = 128
 
 
+def _tensor_key(t: torch.Tensor) -> tuple:
+    """Identity of a tensor's present contents: same storage, same shape, no in-place write
+    since (tensors made under torch.inference_mode keep no version counter)."""
+    try:
+        version = t._version
+    except RuntimeError:
+        version = -1
+    return (t.data_ptr(), tuple(t.shape), t.dtype, version)
+
+
+_unit_scale_seen: dict = {}
+
+
+def _is_unit_scale(scale: torch.Tensor) -> bool:
+    """Whether every scale equals 1.  Reading that back is a device-to-host synchronisation,
+    so it happens once per scale tensor (keyed on its storage and version) and never again:
+    later calls, including calls made while a CUDA graph is being captured, reuse the answer."""
+    key = _tensor_key(scale)
+    hit = _unit_scale_seen.get(key)
+    if hit is None:
+        if len(_unit_scale_seen) > 256:
+            _unit_scale_seen.clear()
+        hit = bool(torch.all(scale == 1.0))
+        _unit_scale_seen[key] = hit
+    return hit
+
+
 def _fold_block_scale(w: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     """w [E, rows, cols] (bf16 or fp8) times scale [E, (rows/128)*(cols/128)] -> bf16."""
-    if w.dtype == torch.bfloat16 and bool(torch.all(scale == 1.0)):
+    if w.dtype == torch.bfloat16 and _is_unit_scale(scale):
         return w
     E, rows, cols = w.shape
+    out = torch.empty((E, rows, cols), dtype=torch.bfloat16, device=w.device)
     s = scale.to(torch.float32).view(E, rows // BLOCK, 1, cols // BLOCK, 1)
-    wf = w.to(torch.float32).view(E, rows // BLOCK, BLOCK, cols // BLOCK, BLOCK) * s
-    return wf.view(E, rows, cols).to(torch.bfloat16).contiguous()
+    for e in range(E):  # per expert: keeps the fp32 temporaries small
+        wf = w[e].to(torch.float32).view(rows // BLOCK, BLOCK, cols // BLOCK, BLOCK) * s[e]
+        out[e] = wf.view(rows, cols).to(torch.bfloat16)
+    return out
 
 
 def _fold_input_scale(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
-    if bool(torch.all(scale == 1.0)):
-        return x
+    """bf16 activations times their per-128 scales, on the device, with no host read."""
     T, H = x.shape
     xf = x.to(torch.float32).view(T, H // BLOCK, BLOCK) * scale.to(torch.float32).unsqueeze(-1)
-    return xf.view(T, H).to(torch.bfloat16).contiguous()
+    return xf.view(T, H).to(torch.bfloat16)
 
 
 class Model:
@@ -74,15 +103,16 @@ class Model:
         self.variant = variant
         self._out_cache: dict = {}
         self._ops: dict = {}
-        self._weight_source = None
+        self._weight_key = None
         self._weights = None
 
     def _prepare_weights(self, w: dict[str, torch.Tensor]):
-        source = (w["w1_q"], w["w2_q"])
-        if self._weights is None or source[0] is not self._weight_source[0] or source[1] is not self._weight_source[1]:
+        # the folded copies depend on the scales as much as on the codes
+        key = tuple(_tensor_key(w[name]) for name in ("w1_q", "fc1_scale", "w2_q", "fc2_scale"))
+        if self._weights is None or key != self._weight_key:
             self._weights = (_fold_block_scale(w["w1_q"], w["fc1_scale"]),
                              _fold_block_scale(w["w2_q"], w["fc2_scale"]))
-            self._weight_source = source
+            self._weight_key = key
         return self._weights
 
     def build_cases(self, *, seq_len: int, shared_input: Any, shared_weights: dict[str, torch.Tensor],
@@ -103,8 +133,9 @@ class Model:
             raise ValueError(f"w1_q shape mismatch: expected {(experts, inter_dim * 2, dim)}, got {tuple(w13.shape)}")
         fp8_in = x.input_q.dtype != torch.bfloat16
         # fp8 activations are dequantised by a kernel inside the timed call (they arrive as
-        # fp8); bf16 activations with non-unit scales are folded once here
-        xin = None if fp8_in else _fold_input_scale(x.input_q, x.input_scale)
+        # fp8); bf16 activations with non-unit scales are scaled inside the call as well
+        # (device arithmetic only), so that the closure always reads the caller's tensor
+        unit_in = fp8_in or _is_unit_scale(x.input_scale)
         dev = x.input_q.device
         key = (seq_len, dim, inter_dim, experts, topk, dev)
         op = self._ops.get(key)
@@ -122,9 +153,16 @@ class Model:
             def run_b200() -> torch.Tensor:
                 _moe.dequant_fp8_rows(xq, xscale, out=xbuf)
                 return op.forward_routed(xbuf, ids, wts, w13, w2)
-        else:
+        elif unit_in:
+            xin = x.input_q.contiguous()
+
             def run_b200() -> torch.Tensor:
                 return op.forward_routed(xin, ids, wts, w13, w2)
+        else:
+            xraw, xscale = x.input_q, x.input_scale
+
+            def run_b200() -> torch.Tensor:
+                return op.forward_routed(_fold_input_scale(xraw, xscale), ids, wts, w13, w2)
 
         return [run_b200]
 

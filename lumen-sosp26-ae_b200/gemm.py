@@ -11,6 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import _cabi
+from ._checks import Operand, check_operands, check_output, require
 
 _workspaces: dict[int, torch.Tensor] = {}
 
@@ -40,42 +41,18 @@ def gemm_pipeline_transposed_b(
     B: torch.Tensor,
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    if A.dtype != torch.bfloat16:
-        raise ValueError(f"A must have dtype torch.bfloat16, got {A.dtype}.")
-    if B.dtype != torch.bfloat16:
-        raise ValueError(f"B must have dtype torch.bfloat16, got {B.dtype}.")
-    if A.ndim != 2:
-        raise ValueError(f"A must be 2D, got shape {tuple(A.shape)}.")
-    if B.ndim != 2:
-        raise ValueError(f"B must be 2D, got shape {tuple(B.shape)}.")
+    op = "gemm_pipeline_transposed_b"
+    dev = check_operands(op, [Operand("A", A, "[M, K]", contiguous=False),
+                              Operand("B", B, "[N, K]", contiguous=False)],
+                         dtype=torch.bfloat16, dtype_error=ValueError)
     m, k = A.shape
     n = B.shape[0]
-    if B.shape[1] != k:
-        raise ValueError(f"B.shape[1] must equal K={k}, got {B.shape[1]}.")
-    if not A.is_cuda or not B.is_cuda:
-        raise ValueError("A and B must be CUDA tensors: this operator has no CPU path.")
-    if B.device != A.device:
-        raise ValueError(f"B must be on device {A.device}, got {B.device}.")
-    if m == 0 or n == 0 or k == 0:
-        raise ValueError(f"empty GEMM is not supported: M={m}, N={n}, K={k}.")
-    if A.stride(1) != 1 or B.stride(1) != 1:
-        raise ValueError("A and B must be row-major (unit stride along K).")
-    if k % 8 != 0 and (A.stride(0) % 8 != 0 or B.stride(0) % 8 != 0):
-        raise ValueError(f"row pitch must be a multiple of 8 elements (16 bytes); K={k}.")
-    if A.stride(0) % 8 != 0 or B.stride(0) % 8 != 0:
-        raise ValueError("row pitch of A and B must be a multiple of 8 elements (16 bytes).")
-
-    out_shape = (m, n)
-    if out is None:
-        out = torch.empty(out_shape, dtype=torch.bfloat16, device=A.device)
-    elif tuple(out.shape) != out_shape:
-        raise ValueError(f"out must have shape {out_shape}, got {tuple(out.shape)}.")
-    elif out.dtype != torch.bfloat16:
-        raise ValueError(f"out must have dtype torch.bfloat16, got {out.dtype}.")
-    elif out.device != A.device:
-        raise ValueError(f"out must be on device {A.device}, got {out.device}.")
-    elif out.stride(1) != 1:
-        raise ValueError("out must be row-major.")
+    require(B.shape[1] == k, op, f"A is [{m}, {k}] and B is {tuple(B.shape)}: both need the same K (B is stored [N, K])")
+    require(m > 0 and n > 0 and k > 0, op, f"nothing to multiply: M={m}, N={n}, K={k}")
+    require(A.stride(0) % 8 == 0 and B.stride(0) % 8 == 0, op,
+            f"rows of A and B must start on 16-byte boundaries (pitch a multiple of 8 elements); "
+            f"pitches are {A.stride(0)} and {B.stride(0)}")
+    out = check_output(op, out, (m, n), dev, dtype=torch.bfloat16, dtype_error=ValueError, contiguous=False)
 
     lib = _cabi.load()
     with _cabi.on_device(A.device):

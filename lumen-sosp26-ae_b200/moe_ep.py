@@ -335,6 +335,8 @@ class PeerExpertParallelMoE:
         self.fused_return = fused_return
         self.row_ptrs = torch.zeros((self.capacity,), dtype=torch.int64, device=device)
         self._flag = torch.zeros((1,), dtype=torch.float32, device=device)
+        # page-locked copy of the device status word, refreshed at the end of every forward
+        self._status_host = torch.zeros((1,), dtype=torch.int32).pin_memory()
         self.rows_hint = max(1, (tokens_local * self.G * topk + experts - 1) // experts)
 
         class _Local:
@@ -354,9 +356,21 @@ class PeerExpertParallelMoE:
                 self.rank, self.G, self._sig_peers, self.epochs.data_ptr(), slot,
                 torch.cuda.current_stream(self.dev).cuda_stream))
 
+    def check_status(self) -> None:
+        """Raises if a kernel of an earlier forward recorded a wait that gave up (e.g. a peer
+        GPU that was more than the barrier's wait limit late).  Reads the page-locked copy the
+        previous forward left behind: no synchronisation, so the newest forward may not be
+        covered yet; device_status() synchronises and covers everything."""
+        code = int(self._status_host[0])
+        if code != 0:
+            raise self._cabi.LumenB200Error(
+                f"expert-parallel forward (status word {code:#x}: site {code >> 16}, "
+                f"slot {(code >> 8) & 0xff}, peer {code & 0xff})", self._cabi.EDEVICE)
+
     def forward(self, x, w13_local, w2_local, *, logits=None, w_router=None, marks=None):
         moe, lib = self.moe, self._cabi.load()
         stream = torch.cuda.current_stream(self.dev).cuda_stream
+        self.check_status()
 
         def mark(label):
             if marks is not None:
@@ -409,5 +423,8 @@ class PeerExpertParallelMoE:
         self._gpu_barrier(2)
         mark("return + barrier")
         out = moe.combine(self.ret, r, self.topk_weights, self.T, out=self.out)
+        with self._cabi.on_device(self.dev):
+            self._cabi.check("lumen_b200_status_snapshot", lib.lumen_b200_status_snapshot(
+                self._status_host.data_ptr(), stream))
         mark("combine")
         return out

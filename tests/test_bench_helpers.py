@@ -24,8 +24,10 @@ def test_sweep_is_the_20_shapes_of_the_configuration():
     assert b.flops([(2, 3, 5)]) == 60.0
     dense = [s for s in shapes if s[0] >= b.DENSE_M]
     assert len(dense) == 8 and b.flops(dense) / b.flops(shapes) > 0.98
-    sample = b.cpu_sample_shapes()
-    assert len(sample) == 12 and all(m <= 128 for m, _, _ in sample)
+    # both arms describe the same work: one config object, 20 shapes, the same FLOPs per step
+    cfg = b.sweep_config(1)
+    assert cfg["shapes"] == 20 and cfg["flop_per_step"] == b.flops(shapes) and cfg["workload"] == b.WORKLOAD
+    assert b.sweep_config(8)["parallelism"].startswith("column-sharded over N x8")
     for world in (2, 4, 8):
         assert all(n % world == 0 for _, n, _ in shapes)
 
@@ -63,3 +65,15 @@ def test_clock_samples_under_load_are_chosen_by_power():
     assert out["reasons"] == ["sw_power_cap"] and out["power_w_max"] == 1001.2
     idle = b.ClockSampler(0)
     assert idle.stop()["reasons"] == ["nvidia-smi unavailable"]
+
+
+def test_operator_records_follow_from_the_work_and_the_time():
+    b = load_bench()
+    peaks = {"bf16_tflops": 1000.0, "hbm_gbs": 5000.0, "source": "measured"}
+    c = {"case": "gemm:1x2x3", "flop": 2.0e12, "bytes": 1.0e9, "launches": 1, "bound": "tensor", "kernel": "k"}
+    rec = b.op_record(c, 4.0, 3.9, peaks, 5)
+    assert rec["tflops"] == 500.0 and rec["roofline"]["frac"] == 0.5 and rec["roofline"]["unit"] == "TFLOP/s"
+    c.update(bound="hbm", tokens=64, experts_touched=3)
+    rec = b.op_record(c, 4.0, 3.9, peaks, 5)
+    assert rec["gbs"] == 250.0 and rec["roofline"]["frac"] == 0.05 and rec["tokens_per_s"] == 16000.0
+    assert set(b.OPS_CASES) <= set(b.CASE_PRESETS)

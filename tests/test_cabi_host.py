@@ -43,19 +43,45 @@ def test_missing_library_fails_loudly(pkg, tmp_path):
         pkg._cabi.load(tmp_path / "liblumen_b200.so")
 
 
-def test_gemm_validation_like_reference(pkg):
+def test_wrappers_raise_the_reference_exception_types(pkg):
+    """What callers can rely on is the exception type per kind of mistake (ValueError for
+    every bad GEMM argument; for attention TypeError on dtypes, ValueError otherwise) and that
+    the message names the wrapper and the offending argument."""
     f = pkg.gemm_pipeline_transposed_b
     a = torch.zeros((4, 8), dtype=torch.bfloat16)
-    with pytest.raises(ValueError, match="A must have dtype torch.bfloat16"):
-        f(a.float(), a)
-    with pytest.raises(ValueError, match="B must have dtype torch.bfloat16"):
-        f(a, a.float())
-    with pytest.raises(ValueError, match="A must be 2D"):
-        f(a[0], a)
-    with pytest.raises(ValueError, match=r"B.shape\[1\] must equal K=8"):
-        f(a, torch.zeros((4, 16), dtype=torch.bfloat16))
-    with pytest.raises(ValueError, match="no CPU path"):
-        f(a, a)
+    for bad_call, word in ((lambda: f(a.float(), a), "A"), (lambda: f(a, a.float()), "B"),
+                           (lambda: f(a[0], a), "A"), (lambda: f(a, a), "CPU")):
+        with pytest.raises(ValueError, match=word) as err:
+            bad_call()
+        assert "gemm_pipeline_transposed_b" in str(err.value)
+    q = torch.zeros((1, 4, 2, 128), dtype=torch.bfloat16)
+    with pytest.raises(TypeError, match="q"):
+        pkg.flash_attn(q.float(), q, q)
+    with pytest.raises(ValueError, match="k"):
+        pkg.flash_attn(q, q[0], q)
+    with pytest.raises(ValueError, match="CPU"):
+        pkg.flash_attn(q, q, q)
+    p3 = torch.zeros((4, 2, 128), dtype=torch.bfloat16)
+    with pytest.raises(TypeError, match="v"):
+        pkg.flash_attn_packed(p3, p3, p3.half(), torch.tensor([0, 4]), 4)
+    with pytest.raises(ValueError, match="flash_attn_packed"):
+        pkg.flash_attn_packed(p3, p3, p3, torch.tensor([0, 4]), 4)  # CPU tensors
+
+
+def test_shared_argument_checker():
+    import importlib
+
+    checks = importlib.import_module("lumen-sosp26-ae_b200._checks")
+    t = torch.zeros((2, 3))
+    with pytest.raises(ValueError, match="2 dimension"):
+        checks.check_operands("op", [checks.Operand("x", t, "[a, b, c]")], dtype=torch.float32, dtype_error=TypeError)
+    with pytest.raises(TypeError, match="float32"):
+        checks.check_operands("op", [checks.Operand("x", t, "[a, b]")], dtype=torch.bfloat16, dtype_error=TypeError)
+    with pytest.raises(ValueError, match="result buffer is"):
+        checks.check_output("op", torch.zeros((2, 2)), (2, 3), t.device, dtype=torch.float32, dtype_error=TypeError)
+    assert checks.check_output("op", None, (2, 3), t.device, dtype=torch.float32, dtype_error=TypeError).shape == (2, 3)
+    with pytest.raises(TypeError, match="op: why"):
+        checks.require(False, "op", "why", TypeError)
 
 
 def test_moe_host_validation(pkg):

@@ -123,3 +123,18 @@ def test_b200_gemm_system_under_the_evaluator(kb):
     assert res.compiled and res.correctness, res.metadata
     assert res.metadata["correctness_trials"] == "(3 / 3)"
     assert res.runtime_stats["timing_mode"] == "cudagraph" and 0 < res.runtime < 5.0 and res.ref_runtime > 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("op", ["attention", "moe"])
+def test_b200_attention_and_moe_systems_under_the_evaluator(kb, op):
+    """ModelNew of the attention and MoE systems through randomised correctness trials and the
+    evaluator's graph-captured timing: the captured call must not read anything back to the
+    host, and new scale tensors in every trial must not meet stale folded weights."""
+    original = REPO / "tests" / "kernelbench" / f"{op}_original.py"
+    system = B200_GEMM.parents[2] / op / "b200" / "model.py"
+    res = kb.evaluate_generated_model(original, system, {"precision": "bf16", "num_correct_trials": 3,
+                                                         "num_trials": 5, "num_warmup": 2})
+    assert res.compiled and res.correctness, res.metadata
+    assert res.metadata["correctness_trials"] == "(3 / 3)"
+    assert res.runtime_stats["timing_mode"] == "cudagraph" and res.runtime > 0
