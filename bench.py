@@ -272,7 +272,22 @@ def measure_ops(args, pkg, dist, dev, rank, world, peaks) -> dict:
         T, _, _, E, _ = (int(x) for x in EP_PRESETS[dims].split("x"))
         if T % world or E % world:
             continue
-        rec = measure_ep(pkg, dist, dev, rank, world, dims, steps=steps, warmup=3, graph=not args.ep_eager)
+        # A failure on one rank (a barrier wait that ran out, a capture that failed) must not
+        # leave the others waiting in a collective: every rank records its outcome, then all
+        # ranks agree on it.
+        try:
+            rec = measure_ep(pkg, dist, dev, rank, world, dims, steps=steps, warmup=3, graph=not args.ep_eager)
+            failed = 0
+        except Exception as exc:  # noqa: BLE001 - reported in the record
+            rec = {"case": f"ep:{dims}", "n_gpus": world, "error": f"{type(exc).__name__}: {exc}"[:300]}
+            failed = 1
+        torch.cuda.synchronize()
+        flag = torch.tensor([failed], device=dev, dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        if int(flag.item()) and "error" not in rec:
+            rec = {"case": f"ep:{dims}", "n_gpus": world, "error": "another rank failed during this case"}
+        if int(flag.item()):
+            pkg.clear_status()
         ops[f"moe_ep_{dims}"] = rec
         torch.cuda.empty_cache()
     return ops
@@ -298,7 +313,9 @@ def run_b200_arm(args) -> None:
         import torch.distributed as dist_mod
 
         dist = dist_mod
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=240))
 
     import __graft_entry__ as entry
 

@@ -48,8 +48,6 @@ constexpr float kLazyRescaleLog2 = 8.0f;
 //   SPLIT    threads per query row in the softmax (1: one warpgroup per query tile, 384
 //            threads; 2: two warpgroups per tile, each thread owns 64 of the 128 keys, 640
 //            threads, so that two warps per scheduler work on a tile's softmax at once)
-//   PACKED   scale/subtract, the polynomial and the row sum use the two-wide fp32
-//            instructions (fma/add .f32x2), which halves their issue slots
 
 enum FaWaitCode {
   kFaWaitQ = 16,
@@ -91,48 +89,7 @@ constexpr size_t fa_smem_bytes() {
   return 1024 + size_t(2 + SLOTS) * kFaTileBytes + sizeof(FaSmemTail<SLOTS>);
 }
 
-// two fp32 values in one 64-bit register pair, for the .f32x2 instructions
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// exp2_fma (sm100_ptx.cuh) of two values at once on the two-wide FMA instructions
-__device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& p0, float& p1) {
-  const uint64_t x = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
-  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t t = f2_add(x, magic);
-  const uint64_t f = f2_sub(x, f2_sub(t, magic));
-  uint64_t p = f2_fma(f, f2_pack(0.0555041087f, 0.0555041087f), f2_pack(0.240226507f, 0.240226507f));
-  p = f2_fma(p, f, f2_pack(0.693147181f, 0.693147181f));
-  p = f2_fma(p, f, f2_pack(1.0f, 1.0f));
-  float t0, t1, q0, q1;
-  f2_unpack(t, t0, t1);
-  f2_unpack(p, q0, q1);
-  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
-}
-
-template <int SLOTS, int SPLIT, int FMA4, bool PACKED>
+template <int SLOTS, int SPLIT, int FMA4>
 __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v, const FaParams prm) {
@@ -426,9 +383,6 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
       const float neg_m = -m * sl2;
       // probabilities p = 2^(s * sl2 - m * sl2); four independent partial sums
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint64_t sum2[2] = {0ull, 0ull};  // PACKED: (sum of p0, sum of p1), (sum of p2, sum of p3)
-      const uint64_t sl2_2 = f2_pack(sl2, sl2);
-      const uint64_t neg_m2 = f2_pack(neg_m, neg_m);
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         // 32 keys -> 16 packed columns, stored to TMEM as soon as they are complete
@@ -436,42 +390,22 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
           const uint32_t* s4 = &sv[c][i];
-          float x0, x1, x2, x3;
-          if constexpr (PACKED) {
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(s4[0]), __uint_as_float(s4[1])), sl2_2, neg_m2), x0, x1);
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(s4[2]), __uint_as_float(s4[3])), sl2_2, neg_m2), x2, x3);
-          } else {
-            x0 = fmaf(__uint_as_float(s4[0]), sl2, neg_m);
-            x1 = fmaf(__uint_as_float(s4[1]), sl2, neg_m);
-            x2 = fmaf(__uint_as_float(s4[2]), sl2, neg_m);
-            x3 = fmaf(__uint_as_float(s4[3]), sl2, neg_m);
-          }
-          float p0, p1, p2, p3;
-          p0 = FMA4 >= 4 ? exp2_fma(x0) : fast_exp2(x0);
-          p1 = FMA4 >= 3 ? exp2_fma(x1) : fast_exp2(x1);
-          if constexpr (PACKED && FMA4 == 2) {
-            exp2_fma_pair(x2, x3, p2, p3);
-          } else {
-            p2 = FMA4 >= 2 ? exp2_fma(x2) : fast_exp2(x2);
-            p3 = FMA4 >= 1 ? exp2_fma(x3) : fast_exp2(x3);
-          }
-          if constexpr (PACKED) {
-            sum2[0] = f2_add(sum2[0], f2_pack(p0, p1));
-            sum2[1] = f2_add(sum2[1], f2_pack(p2, p3));
-          } else {
-            sum4[0] += p0;
-            sum4[1] += p1;
-            sum4[2] += p2;
-            sum4[3] += p3;
-          }
+          const float x0 = fmaf(__uint_as_float(s4[0]), sl2, neg_m);
+          const float x1 = fmaf(__uint_as_float(s4[1]), sl2, neg_m);
+          const float x2 = fmaf(__uint_as_float(s4[2]), sl2, neg_m);
+          const float x3 = fmaf(__uint_as_float(s4[3]), sl2, neg_m);
+          const float p0 = FMA4 >= 4 ? exp2_fma(x0) : fast_exp2(x0);
+          const float p1 = FMA4 >= 3 ? exp2_fma(x1) : fast_exp2(x1);
+          const float p2 = FMA4 >= 2 ? exp2_fma(x2) : fast_exp2(x2);
+          const float p3 = FMA4 >= 1 ? exp2_fma(x3) : fast_exp2(x3);
+          sum4[0] += p0;
+          sum4[1] += p1;
+          sum4[2] += p2;
+          sum4[3] += p3;
           pk[i / 2] = pack_bf16x2(p0, p1);
           pk[i / 2 + 1] = pack_bf16x2(p2, p3);
         }
         tmem_st_32x32b_x16(p_tmem + c * 16, pk);
-      }
-      if constexpr (PACKED) {
-        f2_unpack(sum2[0], sum4[0], sum4[1]);
-        f2_unpack(sum2[1], sum4[2], sum4[3]);
       }
       l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       // my part of P is complete in TMEM: one elected lane per warp tells the MMA thread
@@ -535,11 +469,11 @@ using namespace b200;
 
 namespace {
 
-template <int SPLIT, int FMA4, bool PACKED>
+template <int SPLIT, int FMA4>
 int launch_fa_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FaParams& prm,
                       long long grid, cudaStream_t st) {
   constexpr int kSlots = 4;
-  auto kern = fa_fwd_kernel<kSlots, SPLIT, FMA4, PACKED>;
+  auto kern = fa_fwd_kernel<kSlots, SPLIT, FMA4>;
   constexpr size_t smem = fa_smem_bytes<kSlots>();
   static_assert(smem <= 227 * 1024, "K/V ring does not fit shared memory");
   static bool configured[64] = {};
@@ -597,20 +531,18 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, const int* s
   const long long grid = static_cast<long long>(prm.q_blocks) * B * Hq;
   if (grid <= 0 || grid > 0x7fffffffLL) return LUMEN_B200_EUNSUPPORTED;
   switch (fa_variant()) {
-    case 0:
-      return launch_fa_variant<1, 0, false>(mq, mk, mv, prm, grid, st);
     case 1:
-      return launch_fa_variant<2, 0, false>(mq, mk, mv, prm, grid, st);
+      return launch_fa_variant<1, 1>(mq, mk, mv, prm, grid, st);
     case 2:
-      return launch_fa_variant<2, 1, false>(mq, mk, mv, prm, grid, st);
+      return launch_fa_variant<1, 2>(mq, mk, mv, prm, grid, st);
     case 3:
-      return launch_fa_variant<2, 1, true>(mq, mk, mv, prm, grid, st);
+      return launch_fa_variant<2, 0>(mq, mk, mv, prm, grid, st);
     case 4:
-      return launch_fa_variant<2, 2, true>(mq, mk, mv, prm, grid, st);
+      return launch_fa_variant<2, 1>(mq, mk, mv, prm, grid, st);
     case 5:
-      return launch_fa_variant<2, 0, true>(mq, mk, mv, prm, grid, st);
+      return launch_fa_variant<2, 2>(mq, mk, mv, prm, grid, st);
     default:
-      return launch_fa_variant<2, 2, false>(mq, mk, mv, prm, grid, st);
+      return launch_fa_variant<1, 0>(mq, mk, mv, prm, grid, st);
   }
 }
 

@@ -2,6 +2,7 @@
 // GEMM C = A * B^T and the per-expert (grouped) GEMMs of the MoE.
 #include "gemm_bf16.cuh"
 #include "gemm_bf16_pair.cuh"
+#include "gemm_bf16_pair_grouped.cuh"
 #include <cstdlib>
 #include <string>
 #include "lumen_b200_internal.h"
@@ -58,6 +59,49 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
   const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
   kern<<<2 * clusters, kGemmThreads, smem, st>>>(ma, mb, args);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+// grouped GEMM on CTA pairs (weights on the accumulator rows, tokens on the MMA's N)
+template <int STAGES, bool GATED>
+int launch_gemm_pair_grouped(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& mx_tail,
+                             const GemmArgs& args, cudaStream_t st) {
+  auto kern = gemm_bf16_pair_grouped_kernel<STAGES, GATED>;
+  constexpr size_t smem = gemm_pg_smem_bytes<STAGES, GATED>();
+  static_assert(smem <= 227 * 1024, "stage ring does not fit shared memory");
+  static bool configured[64] = {};
+  static int max_clusters[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LUMEN_B200_ECUDA;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return LUMEN_B200_ECUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = device_sm_count() / 2;
+    }
+    max_clusters[dev] = n;
+    configured[dev] = true;
+  }
+  kern<<<2 * max_clusters[dev], kGemmThreads, smem, st>>>(mw, mx, mx_tail, args);
+  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
+// Grouped GEMMs with many rows per expert: the one-CTA 128 x 256 token-major tiling, or,
+// when the environment variable LUMEN_B200_MOE_TILE says "pair", the CTA-pair kernel with
+// the tokens on the MMA's N.
+bool use_pair_grouped() {
+  static int cached = -1;
+  if (cached < 0) {
+    const char* v = std::getenv("LUMEN_B200_MOE_TILE");
+    cached = (v && v[0] == 'p') ? 1 : 0;
+  }
+  return cached == 1;
 }
 
 // Width of the pair tile.  128-column tiles would cut the idle tail of the last wave in
@@ -277,6 +321,26 @@ static int grouped_gemm_impl(const void* acts, const void* weights, void* out, c
   const uint64_t w_total_rows = uint64_t(E) * w_rows;
   CUtensorMap mp, mq;
   const int grid = sms;
+  if (rows_hint > 128 && use_pair_grouped()) {
+    // CTA pairs: one weight tile x up to 320 token rows per unit, the token count is the MMA's N.
+    // Weight boxes: 128 rows, or for gated units 64 gate rows + 64 up rows; token boxes: 128
+    // rows for the first 256 tokens of a unit and 32 rows for the rest.
+    CUtensorMap mq_tail;
+    {
+      static int unit = 0;  // LUMEN_B200_PG_UNIT=256 keeps every unit to one MMA (measurement aid)
+      if (unit == 0) {
+        const char* v = std::getenv("LUMEN_B200_PG_UNIT");
+        unit = (v && std::atoi(v) >= 16 && std::atoi(v) <= kPgUnitTokens) ? std::atoi(v) : kPgUnitTokens;
+      }
+      args.unit_tokens = unit;
+    }
+    if (encode_tmap_bf16_2d(&mp, weights, w_total_rows, K, K, gated ? kBlockP / 2 : kBlockP) != 0)
+      return LUMEN_B200_ECUDA;
+    if (encode_tmap_bf16_2d(&mq, acts, max_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
+    if (encode_tmap_bf16_2d(&mq_tail, acts, max_rows, K, K, kPgTailBox) != 0) return LUMEN_B200_ECUDA;
+    return gated ? launch_gemm_pair_grouped<5, true>(mp, mq, mq_tail, args, st)
+                 : launch_gemm_pair_grouped<6, false>(mp, mq, mq_tail, args, st);
+  }
   if (rows_hint > 128) {
     // tokens on the TMEM lanes, 128 rows per unit
     if (encode_tmap_bf16_2d(&mp, acts, max_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;

@@ -56,6 +56,7 @@ struct GemmArgs {
   // first element of output row r (possibly in a peer GPU's memory: the epilogue then is the
   // send of the expert-parallel return trip) or nullptr for a row that must not be stored.
   __nv_bfloat16* const* out_row_ptrs;
+  int unit_tokens;  // pair kernel: most token rows one unit takes (256: one MMA; up to 320: two)
   int* status;
 };
 

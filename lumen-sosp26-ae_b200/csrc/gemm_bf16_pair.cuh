@@ -39,6 +39,9 @@ constexpr size_t gemm_pair_smem_bytes() {
   return 1024 + size_t(STAGES) * pair_stage_bytes<BN>() + sizeof(PairSmemTail<STAGES>);
 }
 
+// status code: the two CTAs of a pair were given different TMEM base columns
+enum PairCode { kPairTmemMismatch = 9 };
+
 struct PairUnit {
   int m0, n0;
 };
@@ -97,6 +100,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   tc_fence_after_sync();
 
   const uint32_t tmem_base = tail->tmem_slot;
+  // The leader's MMA addresses the accumulators of both CTAs by the leader's TMEM base, while
+  // each CTA's epilogue reads at its own: the two allocations must have landed on the same
+  // columns.  (They do when no other kernel holds tensor memory on either SM; a mismatch is
+  // reported through the status word and the pair does no work.)
+  if (threadIdx.x == 0 && rank == 1) {
+    const uint32_t leader_base = ld_shared_cluster_u32(map_to_cta(smem_u32(&tail->tmem_slot), 0));
+    if (leader_base != tmem_base) {
+      tail->abort_flag = 1;
+      atomicCAS(args.status, 0, (kPairTmemMismatch << 16) | static_cast<int>(blockIdx.x & 0xffffu));
+    }
+  }
   const int tiles_m = ceil_div(args.M, kPairTileM);
   const int tiles_n = ceil_div(args.N, BN);
   const int total_units = tiles_m * tiles_n;

@@ -251,6 +251,13 @@ __device__ __forceinline__ uint32_t map_to_cta(uint32_t smem_addr, uint32_t cta_
   return r;
 }
 
+// 32-bit load from another CTA's shared memory (address from map_to_cta)
+__device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
 // Plain (non-multicast) tiled load into this CTA's shared memory whose completion is
 // signalled on an mbarrier that may live in the peer CTA of the pair.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst_smem, const CUtensorMap* map,
@@ -383,12 +390,15 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // 2^x on the FMA and integer pipes (no MUFU): split x into the nearest integer j and a
 // fraction f in [-0.5, 0.5], evaluate 2^f with a cubic (relative error below 7e-4, well
 // under the bf16 rounding the result receives) and add j to the exponent field.
-// Inputs below -127 give (denormal) zero.
+// Inputs below -127 give (denormal) zero.  The additions that isolate j are written in PTX:
+// left to the compiler, "x + 1.5 * 2^23 - 1.5 * 2^23" is recognised as a rounding and becomes
+// a conversion instruction, which runs on the same quarter-rate unit as the exp2 it replaces.
 __device__ __forceinline__ float exp2_fma(float x) {
   x = fmaxf(x, -127.0f);
-  const float t = x + 12582912.0f;  // 1.5 * 2^23: the sum's low mantissa bits hold j
-  const float j = t - 12582912.0f;
-  const float f = x - j;
+  float t, j, f;
+  asm("add.rn.f32 %0, %1, 0f4B400000;" : "=f"(t) : "f"(x));  // + 12582912 = 1.5 * 2^23: low mantissa bits hold j
+  asm("sub.rn.f32 %0, %1, 0f4B400000;" : "=f"(j) : "f"(t));
+  asm("sub.rn.f32 %0, %1, %2;" : "=f"(f) : "f"(x), "f"(j));
   float p = fmaf(f, 0.0555041087f, 0.240226507f);
   p = fmaf(p, f, 0.693147181f);
   p = fmaf(p, f, 1.0f);

@@ -169,6 +169,12 @@ class ExpertParallelMoE:
         plan = regroup_plan(both[self.E:].reshape(G, El))
         in_splits = send_splits(counts_h, G)
         self.last_plan, self.last_send_splits = plan, in_splits
+        # The split sizes every rank derives must describe the rows it really holds; a rank
+        # whose counts and rows disagree stops here, before the payload collective (its peers
+        # then run into the process group's timeout instead of receiving misplaced rows).
+        if int(in_splits.sum()) != T * self.k or int(in_splits.sum()) > rows.shape[0]:
+            raise ValueError(f"rank {self.rank}: per-expert counts add up to {int(in_splits.sum())} routes, "
+                             f"but {T} tokens x top-{self.k} = {T * self.k} routes were sorted")
         R = int(plan.recv_splits.sum())
         mark("counts exchange + host plan")
 

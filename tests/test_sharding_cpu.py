@@ -229,6 +229,65 @@ def test_expert_parallel_forward_over_gloo(tmp_path, world, skew):
     assert sorted(p.name for p in tmp_path.iterdir()) == [f"ok{r}" for r in range(world)]
 
 
+# ------------------------------------------------------------------ failures, made on the host
+class _InflatedCounts(OracleOps):
+    """A rank whose per-expert counts do not describe its rows (a corrupted histogram)."""
+
+    def sort(self, ids, wts, experts):
+        r = super().sort(ids, wts, experts)
+        r.expert_counts = r.expert_counts.clone()
+        r.expert_counts[0] += 3
+        return r
+
+
+def _ep_failure_worker(rank, world, port, mode, result_dir):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=6))
+    note = Path(result_dir) / f"rank{rank}"
+    try:
+        ep = importlib.import_module(PKG).moe_ep
+        T, H, I, E, k = 32, 64, 32, 8, 2
+        d = moe_oracle.moe_inputs(T, H, I, E, 7, with_router=False)
+        t0, t1 = rank * T // world, (rank + 1) * T // world
+        el = E // world
+        args = (d["x"][t0:t1], d["w13"][rank * el:(rank + 1) * el], d["w2"][rank * el:(rank + 1) * el])
+        bad = mode == "splits" and rank == 1
+        op = ep.ExpertParallelMoE(experts=E, topk=k, ops=_InflatedCounts(k) if bad else OracleOps(k))
+        try:
+            if mode == "leave":
+                op.forward(*args, logits=d["logits"][t0:t1])  # one good forward together
+                if rank == 1:
+                    note.write_text("left")
+                    return  # leaves between forwards, nothing of its own in flight
+            op.forward(*args, logits=d["logits"][t0:t1])
+            note.write_text("finished")
+        except Exception as exc:  # what the surviving / inconsistent rank must see
+            note.write_text(f"raised:{type(exc).__name__}")
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+@pytest.mark.parametrize("mode", ["splits", "leave"])
+def test_exchange_failures_surface_as_exceptions_not_hangs(tmp_path, mode):
+    """Host-made failures of the collective transport: a rank whose split sizes disagree with
+    its rows raises before it sends anything, a rank that has left makes the next forward of
+    the others raise (process-group timeout or closed connection); nobody returns a result."""
+    world = 2
+    mp.spawn(_ep_failure_worker, args=(world, _free_port(), mode, str(tmp_path)), nprocs=world, join=True)
+    notes = {p.name: p.read_text() for p in tmp_path.iterdir()}
+    if mode == "splits":
+        assert notes["rank1"] == "raised:ValueError"
+        assert notes["rank0"].startswith("raised:")
+    else:
+        assert notes["rank1"] == "left"
+        assert notes["rank0"].startswith("raised:")
+
+
 # ------------------------------------------------------------------ property checks
 def test_exchange_plans_hold_for_random_loads():
     """Random count matrices (empty experts, empty senders, one hot expert): both plans are
