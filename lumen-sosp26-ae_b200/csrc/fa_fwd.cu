@@ -21,33 +21,19 @@
 // reference kernel (datasets/inference/attention/lumen/attn_06_inst_scheduling.py:694-716);
 // probabilities are exp2(s * scale * log2e - m * scale * log2e), rounded to bf16 for the
 // P V product as in the reference (:626,631), and summed in fp32.
-#include <cstdlib>
-
 #include "lumen_b200_internal.h"
 
 namespace b200 {
 
-// 4 copy/MMA warps + two query tiles x SPLIT softmax warpgroups
-__host__ __device__ constexpr int fa_threads(int split) { return 128 + 256 * split; }
-// registers per thread after the setmaxnreg of each role; the launch allocation is
-// 65536 / threads rounded down to a multiple of 8 (168 for 384 threads, 96 for 640)
-__host__ __device__ constexpr int fa_regs_copy(int split) { return split == 1 ? 72 : 56; }
-__host__ __device__ constexpr int fa_regs_softmax(int split) { return split == 1 ? 216 : 104; }
-static_assert(128 * fa_regs_copy(1) + 256 * fa_regs_softmax(1) <= 384 * 168, "register file budget");
-static_assert(128 * fa_regs_copy(2) + 512 * fa_regs_softmax(2) <= 640 * 96, "register file budget");
+constexpr int kFaThreads = 384;      // 4 copy/MMA warps + one softmax warpgroup per query tile
+constexpr int kFaRegsCopy = 72;      // registers per thread kept by the copy/MMA warpgroup
+constexpr int kFaRegsSoftmax = 216;  // registers per thread taken by the softmax warpgroups
+static_assert(128 * kFaRegsCopy + 256 * kFaRegsSoftmax <= 384 * 168, "register file budget");
 constexpr int kFaTile = 128;     // query rows per tile and keys per KV tile
 constexpr int kFaD = 128;        // head dimension
 constexpr int kFaHalfBytes = kFaTile * 64 * 2;   // one [128][64] bf16 swizzled panel
 constexpr int kFaTileBytes = 2 * kFaHalfBytes;   // one [128][128] tile = two panels
 constexpr float kLazyRescaleLog2 = 8.0f;
-
-// Compile-time choices of the softmax -> P V hand-off, template parameters of the kernel:
-//   FMA4     of every four exp2, this many run as a polynomial on the FMA pipe instead of the
-//            MUFU (the MUFU issues one warp instruction per 8 cycles, which bounds a softmax
-//            warp at 1024 cycles per 128 columns when every exp2 goes there)
-//   SPLIT    threads per query row in the softmax (1: one warpgroup per query tile, 384
-//            threads; 2: two warpgroups per tile, each thread owns 64 of the 128 keys, 640
-//            threads, so that two warps per scheduler work on a tile's softmax at once)
 
 enum FaWaitCode {
   kFaWaitQ = 16,
@@ -56,7 +42,6 @@ enum FaWaitCode {
   kFaWaitS = 19,
   kFaWaitP = 20,
   kFaWaitO = 21,
-  kFaWaitRow = 22,
 };
 
 struct FaParams {
@@ -77,11 +62,8 @@ struct FaSmemTail {
   uint64_t s_ready[2];
   uint64_t p_ready[2];
   uint64_t o_done[2];
-  uint64_t row_xchg[2][4];  // [query tile][lane quadrant]: the warps that share those rows meet here
   uint32_t tmem_slot;
   int abort_flag;
-  float row_max[2 * 2 * kFaTile];  // [query tile][part][row] partial row maxima of one step
-  float row_sum[2 * 2 * kFaTile];  // the same for the final row sums
 };
 
 template <int SLOTS>
@@ -89,8 +71,8 @@ constexpr size_t fa_smem_bytes() {
   return 1024 + size_t(2 + SLOTS) * kFaTileBytes + sizeof(FaSmemTail<SLOTS>);
 }
 
-template <int SLOTS, int SPLIT, int FMA4>
-__global__ void __launch_bounds__(fa_threads(SPLIT), 1)
+template <int SLOTS>
+__global__ void __launch_bounds__(kFaThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v, const FaParams prm) {
   using Tail = FaSmemTail<SLOTS>;
@@ -142,9 +124,8 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&tail->s_ready[t]), 1);
-      mbar_init(smem_u32(&tail->p_ready[t]), 4 * SPLIT);  // one elected lane per softmax warp
+      mbar_init(smem_u32(&tail->p_ready[t]), 4);  // one elected lane per softmax warp
       mbar_init(smem_u32(&tail->o_done[t]), 1);
-      for (int q = 0; q < 4; ++q) mbar_init(smem_u32(&tail->row_xchg[t][q]), SPLIT);
     }
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -161,8 +142,8 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
   // Registers: the copy/MMA warpgroup gives most of its launch allocation back, the softmax
   // warpgroups take it (each role branch below starts with its own setmaxnreg so that the
   // register bound of a branch is visible to the compiler).
-  constexpr int kRegsCopy = fa_regs_copy(SPLIT);
-  constexpr int kRegsSoftmax = fa_regs_softmax(SPLIT);
+  constexpr int kRegsCopy = kFaRegsCopy;
+  constexpr int kRegsSoftmax = kFaRegsSoftmax;
   if (warp == 0) {
     // ================================ TMA producer ======================================
     reg_dealloc<kRegsCopy>();
@@ -274,48 +255,80 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
     reg_dealloc<kRegsCopy>();
   } else {
     // ================================ softmax + epilogue ================================
-    // SPLIT threads share a row: thread `part` owns the kCols consecutive keys / output
-    // columns [part * kCols, +kCols) of it.  The SPLIT warps of one (tile, lane quadrant)
-    // exchange their partial row maxima and sums through shared memory.
     reg_alloc<kRegsSoftmax>();
-    constexpr int kCols = kFaTile / SPLIT;
-    constexpr int kChunks = kCols / 32;
-    const int sw = warp - 4;
-    const int t = sw / (4 * SPLIT);         // query tile of this warp
-    const int part = (sw >> 2) % SPLIT;     // which columns of the row
+    const int t = (warp - 4) >> 2;          // query tile of this warpgroup
     const int quad = warp & 3;              // TMEM lane quadrant
     const int r = quad * 32 + lane;         // row of the tile
     const int q = q0 + t * kFaTile + r;     // query position
     const int n = n_tiles[t];
     const uint32_t lane_sel = uint32_t(quad * 32) << 16;
-    const uint32_t s_tmem = tmem_base + lane_sel + t * 128 + part * kCols;        // my S columns
-    const uint32_t p_tmem = tmem_base + lane_sel + t * 128 + part * (kCols / 2);  // my packed P columns
-    const uint32_t o_tmem = tmem_base + lane_sel + 256 + t * 128 + part * kCols;  // my O columns
+    const uint32_t s_tmem = tmem_base + lane_sel + t * 128;        // scores; packed P overwrites columns 0..63
+    const uint32_t o_tmem = tmem_base + lane_sel + 256 + t * 128;  // output accumulator
     const float sl2 = prm.scale_log2;
     // last key this row may see
     const int kv_lim = prm.causal ? min(q, seq_len - 1) : seq_len - 1;
-    const uint32_t xbar = smem_u32(&tail->row_xchg[t][quad]);
-    uint32_t xphase = 0;
-    // value of the row's other part(s): publish mine, meet, read theirs
-    auto row_exchange = [&](float* slots, float mine, auto combine, bool& ok) {
-      if constexpr (SPLIT == 1) {
-        return mine;
-      } else {
-        slots[(t * SPLIT + part) * kFaTile + r] = mine;
+
+    float m = -INFINITY;  // maximum the probabilities are taken against (raw score units)
+    float l = 0.f;        // running sum of probabilities
+    bool ok = true;
+
+    // raise m to m_new: O and l shrink by 2^((m - m_new) * sl2).  O of step j - 1 must be complete.
+    auto raise_max = [&](float m_new, int j) {
+      const float factor = fast_exp2((m - m_new) * sl2);  // 0 on the first tile
+      m = m_new;
+      l *= factor;
+      if (j > 0) {
+        if (!mbar_wait(smem_u32(&tail->o_done[t]), (j - 1) & 1, ctx, kFaWaitO)) return false;
         __syncwarp();
-        if (lane == 0) mbar_arrive(xbar);
-        if (!mbar_wait(xbar, xphase, ctx, kFaWaitRow)) ok = false;
-        xphase ^= 1u;
-        float v = mine;
+        tc_fence_after_sync();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_tmem + c * 32, ov);
+          tmem_ld_wait();
 #pragma unroll
-        for (int o = 1; o < SPLIT; ++o) v = combine(v, slots[(t * SPLIT + ((part + o) % SPLIT)) * kFaTile + r]);
-        return v;
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * factor);
+          tmem_st_32x32b_x32(o_tmem + c * 32, ov);
+        }
+        tmem_st_wait();
       }
+      return true;
+    };
+    // maximum of 32 scores: independent chains of three-input max
+    auto chunk_max = [](const uint32_t (&s)[32]) {
+      float a = max3(__uint_as_float(s[0]), __uint_as_float(s[1]), __uint_as_float(s[2]));
+      float b2 = max3(__uint_as_float(s[3]), __uint_as_float(s[4]), __uint_as_float(s[5]));
+#pragma unroll
+      for (int i = 6; i + 3 < 32; i += 4) {
+        a = max3(a, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+        b2 = max3(b2, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
+      }
+      return max3(a, b2, fmaxf(__uint_as_float(s[30]), __uint_as_float(s[31])));
+    };
+    // 32 scores -> probabilities 2^(s * sl2 + neg_m), packed to 16 bf16x2 columns at P group c
+    auto emit_chunk = [&](const uint32_t (&s)[32], int c, float neg_m, float (&sum4)[4]) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float p0 = fast_exp2(fmaf(__uint_as_float(s[i + 0]), sl2, neg_m));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(s[i + 1]), sl2, neg_m));
+        const float p2 = fast_exp2(fmaf(__uint_as_float(s[i + 2]), sl2, neg_m));
+        const float p3 = fast_exp2(fmaf(__uint_as_float(s[i + 3]), sl2, neg_m));
+        sum4[0] += p0;
+        sum4[1] += p1;
+        sum4[2] += p2;
+        sum4[3] += p3;
+        pk[i / 2] = pack_bf16x2(p0, p1);
+        pk[i / 2 + 1] = pack_bf16x2(p2, p3);
+      }
+      tmem_st_32x32b_x16(s_tmem + c * 16, pk);
+    };
+    auto mask_chunk = [](uint32_t (&s)[32], int first_col, int cmax) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (first_col + i > cmax) s[i] = __float_as_uint(-INFINITY);
     };
 
-    float m = -INFINITY;  // running maximum (raw score units)
-    float l = 0.f;        // running sum of this thread's probabilities
-    bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
       if (!mbar_wait(smem_u32(&tail->s_ready[t]), j & 1, ctx, kFaWaitS)) {
         ok = false;
@@ -323,92 +336,32 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
       }
       __syncwarp();
       tc_fence_after_sync();
-      uint32_t sv[kChunks][32];
-#pragma unroll
-      for (int c = 0; c < kChunks; ++c) tmem_ld_32x32b_x32(s_tmem + c * 32, sv[c]);
-      tmem_ld_wait();
-
-      const int cmax = kv_lim - j * kFaTile - part * kCols;  // my columns [0, cmax] are visible
-      if (cmax < kCols - 1) {
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i > cmax) sv[c][i] = __float_as_uint(-INFINITY);
-      }
-      // row maximum: independent chains of three-input max
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        float a = max3(__uint_as_float(sv[c][0]), __uint_as_float(sv[c][1]), __uint_as_float(sv[c][2]));
-#pragma unroll
-        for (int i = 3; i + 1 < 32; i += 2)
-          a = max3(a, __uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1]));
-        mx = fmaxf(mx, fmaxf(a, __uint_as_float(sv[c][31])));
-      }
-      // After this meeting every part has its S columns in registers, so the packed P of a
-      // later part may overwrite the S columns of an earlier one.
-      mx = row_exchange(tail->row_max, mx, [](float a, float b2) { return fmaxf(a, b2); }, ok);
-      if (!ok) break;
-
-      // lazy rescale: raise m only when the tile maximum is far above it (warp-uniform,
-      // because the O update below is a warp-collective TMEM access; the parts of a row
-      // see the same maximum, so their warps decide alike)
-      const bool need = (mx - m) * sl2 > kLazyRescaleLog2;
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_new = fmaxf(m, mx);
-        const float factor = fast_exp2((m - m_new) * sl2);  // 0 on the first tile
-        m = m_new;
-        l *= factor;
-        if (j > 0) {
-          if (!mbar_wait(smem_u32(&tail->o_done[t]), (j - 1) & 1, ctx, kFaWaitO)) {
-            ok = false;
-            break;
-          }
-          __syncwarp();
-          tc_fence_after_sync();
-#pragma unroll 1
-          for (int c = 0; c < kChunks; ++c) {
-            uint32_t ov[32];
-            tmem_ld_32x32b_x32(o_tmem + c * 32, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * factor);
-            tmem_st_32x32b_x32(o_tmem + c * 32, ov);
-          }
-          tmem_st_wait();
-        }
-      }
-
-      const float neg_m = -m * sl2;
-      // probabilities p = 2^(s * sl2 - m * sl2); four independent partial sums
+      uint32_t sv[4][32];
+      const int cmax = kv_lim - j * kFaTile;  // columns [0, cmax] are visible
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+
+      // whole row first: maximum, lazy rescale, then the probabilities
 #pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        // 32 keys -> 16 packed columns, stored to TMEM as soon as they are complete
-        uint32_t pk[16];
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_tmem + c * 32, sv[c]);
+      tmem_ld_wait();
+      if (cmax < kFaTile - 1) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const uint32_t* s4 = &sv[c][i];
-          const float x0 = fmaf(__uint_as_float(s4[0]), sl2, neg_m);
-          const float x1 = fmaf(__uint_as_float(s4[1]), sl2, neg_m);
-          const float x2 = fmaf(__uint_as_float(s4[2]), sl2, neg_m);
-          const float x3 = fmaf(__uint_as_float(s4[3]), sl2, neg_m);
-          const float p0 = FMA4 >= 4 ? exp2_fma(x0) : fast_exp2(x0);
-          const float p1 = FMA4 >= 3 ? exp2_fma(x1) : fast_exp2(x1);
-          const float p2 = FMA4 >= 2 ? exp2_fma(x2) : fast_exp2(x2);
-          const float p3 = FMA4 >= 1 ? exp2_fma(x3) : fast_exp2(x3);
-          sum4[0] += p0;
-          sum4[1] += p1;
-          sum4[2] += p2;
-          sum4[3] += p3;
-          pk[i / 2] = pack_bf16x2(p0, p1);
-          pk[i / 2 + 1] = pack_bf16x2(p2, p3);
-        }
-        tmem_st_32x32b_x16(p_tmem + c * 16, pk);
+        for (int c = 0; c < 4; ++c) mask_chunk(sv[c], c * 32, cmax);
       }
+      const float mx = fmaxf(fmaxf(chunk_max(sv[0]), chunk_max(sv[1])), fmaxf(chunk_max(sv[2]), chunk_max(sv[3])));
+      // lazy rescale: raise m only when the tile maximum is far above it (warp-uniform,
+      // because the O update is a warp-collective TMEM access)
+      if (__any_sync(0xffffffffu, (mx - m) * sl2 > kLazyRescaleLog2)) {
+        if (!raise_max(fmaxf(m, mx), j)) {
+          ok = false;
+          break;
+        }
+      }
+      const float neg_m = -m * sl2;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) emit_chunk(sv[c], c, neg_m, sum4);
       l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-      // my part of P is complete in TMEM: one elected lane per warp tells the MMA thread
+      // P is complete in TMEM: one elected lane per warp tells the MMA thread
       tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();
@@ -416,20 +369,14 @@ __global__ void __launch_bounds__(fa_threads(SPLIT), 1)
     }
 
     // ---- epilogue: O / l -> bf16 -> global -------------------------------------------
-    if (n > 0) {
-      bool met = true;  // every part takes this meeting, also after a wait gave up
-      l = row_exchange(tail->row_sum, l, [](float a, float b2) { return a + b2; }, met);
-      ok = ok && met;
-    }
     if (ok && n > 0) {
       if (mbar_wait(smem_u32(&tail->o_done[t]), (n - 1) & 1, ctx, kFaWaitO)) {
         __syncwarp();
         tc_fence_after_sync();
         const float inv_l = 1.0f / l;
-        __nv_bfloat16* orow =
-            prm.O + ((size_t(row_base) + q) * prm.Hq + hq) * kFaD + part * kCols;
+        __nv_bfloat16* orow = prm.O + ((size_t(row_base) + q) * prm.Hq + hq) * kFaD;
 #pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
           tmem_ld_32x32b_x32(o_tmem + c * 32, ov);
           tmem_ld_wait();
@@ -469,11 +416,10 @@ using namespace b200;
 
 namespace {
 
-template <int SPLIT, int FMA4>
-int launch_fa_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FaParams& prm,
-                      long long grid, cudaStream_t st) {
+int launch_fa_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FaParams& prm,
+                     long long grid, cudaStream_t st) {
   constexpr int kSlots = 4;
-  auto kern = fa_fwd_kernel<kSlots, SPLIT, FMA4>;
+  auto kern = fa_fwd_kernel<kSlots>;
   constexpr size_t smem = fa_smem_bytes<kSlots>();
   static_assert(smem <= 227 * 1024, "K/V ring does not fit shared memory");
   static bool configured[64] = {};
@@ -485,19 +431,8 @@ int launch_fa_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtens
       return LUMEN_B200_ECUDA;
     configured[dev] = true;
   }
-  kern<<<static_cast<unsigned>(grid), fa_threads(SPLIT), smem, st>>>(mq, mk, mv, prm);
+  kern<<<static_cast<unsigned>(grid), kFaThreads, smem, st>>>(mq, mk, mv, prm);
   return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
-}
-
-// Which instantiation runs.  LUMEN_B200_FA_VARIANT (a digit, read once) selects one of the
-// measured alternatives; unset = the default.
-int fa_variant() {
-  static int cached = -1;
-  if (cached < 0) {
-    const char* v = std::getenv("LUMEN_B200_FA_VARIANT");
-    cached = (v && v[0] >= '0' && v[0] <= '9') ? v[0] - '0' : 0;
-  }
-  return cached;
 }
 
 // rows = packed tokens; S_max = longest sequence (sizes the grid)
@@ -530,20 +465,7 @@ int launch_fa(const void* Q, const void* K, const void* V, void* O, const int* s
 
   const long long grid = static_cast<long long>(prm.q_blocks) * B * Hq;
   if (grid <= 0 || grid > 0x7fffffffLL) return LUMEN_B200_EUNSUPPORTED;
-  switch (fa_variant()) {
-    case 1:
-      return launch_fa_variant<1, 1>(mq, mk, mv, prm, grid, st);
-    case 2:
-      return launch_fa_variant<1, 2>(mq, mk, mv, prm, grid, st);
-    case 3:
-      return launch_fa_variant<2, 0>(mq, mk, mv, prm, grid, st);
-    case 4:
-      return launch_fa_variant<2, 1>(mq, mk, mv, prm, grid, st);
-    case 5:
-      return launch_fa_variant<2, 2>(mq, mk, mv, prm, grid, st);
-    default:
-      return launch_fa_variant<1, 0>(mq, mk, mv, prm, grid, st);
-  }
+  return launch_fa_kernel(mq, mk, mv, prm, grid, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }

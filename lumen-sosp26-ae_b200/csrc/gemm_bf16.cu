@@ -10,6 +10,30 @@
 namespace b200 {
 namespace {
 
+// Launch with programmatic stream serialization: the kernel may begin (up to its
+// griddep_wait()) before the previous kernel of the stream has finished.  Every kernel
+// launched through here waits before it touches global memory.  LUMEN_B200_PDL=0 turns the
+// attribute off (measurement aid).
+template <typename Kern, typename... Args>
+int launch_overlapped(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  static int pdl = -1;
+  if (pdl < 0) {
+    const char* v = std::getenv("LUMEN_B200_PDL");
+    pdl = (v && v[0] == '0') ? 0 : 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+}
+
 template <int BN, int STAGES, bool SWAP, bool GATED, bool GROUPED>
 int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& args, int grid,
                 cudaStream_t st) {
@@ -25,8 +49,7 @@ int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& ar
       return LUMEN_B200_ECUDA;
     configured[dev] = true;
   }
-  kern<<<grid, kGemmThreads, smem, st>>>(mp, mq, args);
-  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+  return launch_overlapped(kern, dim3(grid), dim3(kGemmThreads), smem, st, mp, mq, args);
 }
 
 // dense GEMM on CTA pairs (clusters of 2); grid = 2 CTAs per co-resident cluster
@@ -57,8 +80,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
     configured[dev] = true;
   }
   const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
-  kern<<<2 * clusters, kGemmThreads, smem, st>>>(ma, mb, args);
-  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+  return launch_overlapped(kern, dim3(2 * clusters), dim3(kGemmThreads), smem, st, ma, mb, args);
 }
 
 // grouped GEMM on CTA pairs (weights on the accumulator rows, tokens on the MMA's N)
@@ -88,8 +110,7 @@ int launch_gemm_pair_grouped(const CUtensorMap& mw, const CUtensorMap& mx, const
     max_clusters[dev] = n;
     configured[dev] = true;
   }
-  kern<<<2 * max_clusters[dev], kGemmThreads, smem, st>>>(mw, mx, mx_tail, args);
-  return cudaGetLastError() == cudaSuccess ? LUMEN_B200_OK : LUMEN_B200_ECUDA;
+  return launch_overlapped(kern, dim3(2 * max_clusters[dev]), dim3(kGemmThreads), smem, st, mw, mx, mx_tail, args);
 }
 
 // Grouped GEMMs with many rows per expert: the one-CTA 128 x 256 token-major tiling, or,

@@ -260,6 +260,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tmem_alloc(smem_u32(&tail->tmem_slot), Cfg::kTmemCols);
   }
+  // nothing above reads or writes global memory: it may overlap the previous kernel's tail
+  griddep_wait();
+  griddep_launch_dependents();
   if constexpr (GROUPED) {
     // unit_start[e] = (weight tiles) * (activation tiles of experts before e); warp 0 scans
     if (warp == 0) {

@@ -94,6 +94,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&map_b);
   }
   if (warp == 1) tmem_alloc(smem_u32(&tail->tmem_slot), kTmemCols);
+  // nothing above reads or writes global memory: it may overlap the previous kernel's tail
+  griddep_wait();
+  griddep_launch_dependents();
   tc_fence_before_sync();
   __syncthreads();
   cluster_sync_all();  // barriers of both CTAs are initialised before any remote arrival

@@ -132,6 +132,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&map_x_tail);
   }
   if (warp == 1) tmem_alloc(smem_u32(&tail->tmem_slot), 512);
+  // nothing above reads or writes global memory: it may overlap the previous kernel's tail
+  griddep_wait();
+  griddep_launch_dependents();
   // units of expert e: (weight tiles) x (token tiles of at most 320 rows); warp 0 scans
   const int w_tiles = ceil_div(args.N, kOutCols);
   if (warp == 0) {

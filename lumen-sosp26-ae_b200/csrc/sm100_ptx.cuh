@@ -135,6 +135,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst_smem, const CUtensorMap
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with the programmatic-serialization
+// attribute may start while its predecessor in the stream is still running; everything it does
+// before griddep_wait() (barrier initialisation, TMEM allocation, descriptor prefetch) then
+// overlaps the predecessor's tail.  griddep_wait() returns once the predecessor grid has
+// completed and its memory is visible; without the attribute both calls do nothing.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // tcgen05: tensor memory management
 // ---------------------------------------------------------------------------
 // Whole-warp calls (.sync.aligned).  ncols: power of two in [32, 512].
