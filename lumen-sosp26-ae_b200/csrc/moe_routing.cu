@@ -362,10 +362,11 @@ __global__ void __launch_bounds__(kRouteChunk)
   }
   __syncthreads();
 
-  // stable rank among the routes of the same expert, then scatter
-  const int warp_last = tid | 31;
+  // stable rank among the routes of the same expert, then scatter (threads past the last
+  // route have nothing to rank: with a handful of routes the loop is a handful of steps)
   int rank = 0;
-  for (int j = 0; j < warp_last; ++j) rank += (j < tid && s_e[j] == e) ? 1 : 0;
+  if (e >= 0)
+    for (int j = 0; j < tid; ++j) rank += (s_e[j] == e) ? 1 : 0;
   if (e >= 0) {
     const int pos = s_off[e] + rank;
     const int token = tid / k;
