@@ -536,7 +536,12 @@ CASE_PRESETS = {
     "c5_t64": "moe:64x7168x2048x256x8", "c5_t512": "moe:512x7168x2048x256x8",
     "c5_t8192": "moe:8192x7168x2048x256x8",
 }
-OPS_CASES = ("c1", "c3a", "c3b", "c4", "c5_t1", "c5_t64", "c5_t512", "c5_t8192")
+CASE_PRESETS.update({"fp8_t64": "moe8:64x7168x2048x32x4", "fp8_t512": "moe8:512x7168x2048x32x4",
+                     "bf16_t64": "moe:64x7168x2048x32x4", "bf16_t512": "moe:512x7168x2048x32x4"})
+# the metric's five configurations, then the reference's own MoE format (fp8 codes + block scales,
+# its table shape: 32 experts, top-4) beside the same shape in bf16
+OPS_CASES = ("c1", "c3a", "c3b", "c4", "c5_t1", "c5_t64", "c5_t512", "c5_t8192",
+             "bf16_t64", "bf16_t512", "fp8_t64", "fp8_t512")
 
 
 class CaseBuilder:
@@ -612,6 +617,36 @@ class CaseBuilder:
                      stages=lambda: op.stage_times(x, w13, w2, w_router=w_router, logits=logits),
                      stage_work={"gemm_w13_silu": (4.0 * T * K * H * I, 2.0 * 2 * I * H * touched),
                                  "gemm_w2": (2.0 * T * K * H * I, 2.0 * H * I * touched)})
+        elif kind == "moe8":
+            # fp8 e4m3 codes + fp32 block scales with the harness' distributions
+            # (scripts/benchmark/backend_moe.py:86-210), through the fp8 tensor-core kernels
+            T, H, I, E, K = (int(x) for x in parts[:5])
+            f8 = t.float8_e4m3fn
+            rnd = lambda shape: t.randn(shape, device=self.dev, dtype=t.float32, generator=self.g)  # noqa: E731
+            x_q = (rnd((T, H)) + 0.1).to(f8)
+            x_s = (rnd((T, H // 128)) * 2e-2 + 1e-1).clamp_min_(1e-8)
+            tv, ti = t.topk(rnd((T, E)), k=K, dim=-1)
+            ids, wts = ti.to(t.int32).contiguous(), t.softmax(tv, dim=-1).contiguous()
+            key = ("f8", E, H, I)
+            if key not in self._weights:
+                self._weights.clear()
+                w13 = t.empty((E, 2 * I, H), device=self.dev, dtype=f8)
+                w2 = t.empty((E, H, I), device=self.dev, dtype=f8)
+                for e in range(E):
+                    w13[e] = (rnd((2 * I, H)) * 8.0).to(f8)
+                    w2[e] = (rnd((H, I)) * 8.0).to(f8)
+                s13 = (rnd((E, (2 * I // 128) * (H // 128))) * 2e-3 + 1e-2).clamp_min_(1e-8)
+                s2 = (rnd((E, (H // 128) * (I // 128))) * 2e-3 + 1e-2).clamp_min_(1e-8)
+                self._weights[key] = (w13, s13, w2, s2)
+            w13, s13, w2, s2 = self._weights[key]
+            op = pkg.moe.FusedMoEFp8(tokens=T, hidden=H, inter=I, experts=E, topk=K, device=self.dev)
+            call = lambda: op.forward_routed(x_q, x_s, ids, wts, w13, s13, w2, s2)  # noqa: E731
+            call()
+            t.cuda.synchronize()
+            touched = int((op.routes.expert_counts > 0).sum().item())
+            c.update(call=call, flop=6.0 * T * K * H * I, bytes=3.0 * H * I * touched + T * H + 2.0 * T * H,
+                     launches=6, bound="hbm", kernel="moe_fp8_grouped_kernel (kind::f8f6f4)", tokens=T,
+                     experts_touched=touched)
         else:
             raise SystemExit(f"unknown case {case!r}")
         return c

@@ -231,6 +231,44 @@ int lumen_b200_moe_forward(const void* x, const void* w13, const void* w2, const
 int lumen_b200_moe_dequant_fp8(const void* q, const void* scale, const void* lut, void* out, int T,
                                int H, void* stream);
 
+/* ------------------------------------------------ MoE, fp8 block-scale -- */
+/* The reference's own data format: fp8 e4m3 codes with fp32 scales per 1 x 128 block of an
+ * activation row and per 128 x 128 block of a weight matrix
+ * (scripts/benchmark/backend_moe.py:86-210).  The products run on the tensor cores in fp8
+ * (tcgen05.mma.kind::f8f6f4); each 128-wide K block's partial sum is multiplied by
+ * act_scale * w_scale while it is added to an fp32 accumulator, as the reference kernel does
+ * (datasets/inference/moe/lumen/fused_moe.py:400-443). */
+
+/* scale_t[kb, pos] (fp32, [KB, max_rows]) = scale[token(sorted_token_ids[pos]), kb] for
+ * pos < num_valid_ids[0], 1 elsewhere: the activation scales [T, KB] gathered into expert
+ * order and stored K-block-major, the layout the reference kernel reads too
+ * (datasets/inference/moe/lumen/model.py:259).  The codes themselves are gathered with
+ * lumen_b200_moe_permute_rows (a row of H codes = H / 2 two-byte elements). */
+int lumen_b200_moe_gather_scales_t(const void* scale, const void* sorted_token_ids,
+                                   const void* num_valid_ids, void* out_t, int T, int KB, int max_rows,
+                                   void* stream);
+
+/* Per-expert GEMM over fp8 rows in expert order:
+ *   acts_q [max_rows, K] codes, act_scale_t [K/128, max_rows] fp32;
+ *   weights_q [E, w_rows, K] codes (w_rows = N, or 2N gate rows first for gated != 0),
+ *   w_scale [E, w_rows/128, K/128] fp32 (the fc1_scale / fc2_scale layout of the harness).
+ *   gated == 0:                     out bf16 [max_rows, N]
+ *   gated != 0, quantize_out == 0:  out bf16 [max_rows, N] = silu(gate) * up
+ *   gated != 0, quantize_out != 0:  out = fp8 codes [max_rows, N] of silu(gate) * up, re-quantised
+ *                                   per row and 128-column block (scale = block maximum / 448,
+ *                                   out_scale_t [N/128, max_rows]) for the second GEMM -- the
+ *                                   per-row re-quantisation of the reference kernel
+ *                                   (datasets/inference/moe/lumen/fused_moe.py:684-788).
+ * N % 128 == 0 and K % 128 == 0 (whole scale blocks, as scripts/benchmark/backend_moe.py:77-83
+ * requires).  Codes are OCP e4m3; every product is also multiplied by scale_mul, which is how
+ * e4m3fnuz inputs are taken: the same bits mean half the value, so pass 0.5 per fnuz operand.
+ * rows_hint = expected rows per expert (0 = unknown), picks the token tile. */
+int lumen_b200_moe_grouped_gemm_fp8(const void* acts_q, const void* act_scale_t, const void* weights_q,
+                                    const void* w_scale, void* out, void* out_scale_t,
+                                    const void* expert_offsets, const void* expert_counts, int max_rows,
+                                    int E, int N, int K, int gated, int quantize_out, float scale_mul,
+                                    int rows_hint, void* stream);
+
 /* ---------------------------------------------- MoE, expert parallel (G GPUs) -- */
 /* Tokens and experts are sharded over G GPUs (expert e on GPU e / (E/G)); each GPU sorts
  * its own routes compactly (route_group = 1).  `counts` is the G x E matrix of every

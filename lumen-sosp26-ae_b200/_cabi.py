@@ -96,6 +96,13 @@ SIGNATURES = {
     ),
     "lumen_b200_moe_dequant_fp8": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "lumen_b200_moe_gather_scales_t": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "lumen_b200_moe_grouped_gemm_fp8": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+         c_int, c_int, c_int, c_float, c_int, c_void_p],
+    ),
     "lumen_b200_moe_ep_barrier": (
         c_int, [c_int, c_int, ctypes.POINTER(c_void_p), c_void_p, c_int, c_void_p]),
     "lumen_b200_moe_ep_exchange_counts": (

@@ -27,6 +27,11 @@ int* device_status_word();
 int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                         uint64_t ld_elems, uint32_t box_rows);
 
+// 2-D row-major tensor map over bytes (fp8 codes) with a {128 x box_rows} box and the 128-byte
+// swizzle; `ld_bytes` is the row pitch (a multiple of 16).  Returns 0 on success.
+int encode_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                      uint32_t box_rows);
+
 // General bf16 tensor map, rank <= 4, 128-byte swizzle; dims/strides innermost first,
 // strides in bytes for dims 1..rank-1.
 int encode_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,

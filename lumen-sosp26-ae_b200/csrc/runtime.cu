@@ -80,6 +80,20 @@ int encode_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_
   return r == CUDA_SUCCESS ? 0 : -1;
 }
 
+int encode_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                      uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstr[1] = {ld_bytes};
+  const cuuint32_t bdim[2] = {128, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstr, bdim, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return res == CUDA_SUCCESS ? 0 : -1;
+}
+
 int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                         uint64_t ld_elems, uint32_t box_rows) {
   const uint64_t dims[2] = {cols, rows};

@@ -6,12 +6,21 @@
 `Model(variant=...).build_cases(...)` follows the case-backend contract
 (scripts/benchmark/backend_moe.py:263-336): it receives the harness' precomputed routing
 (topk_ids, topk_weights) and returns zero-argument callables.  `ModelNew.forward` follows
-the python-backend contract (:339-403).  The expert GEMMs compute in bf16.  The harness'
-weight block scales (fc1_scale, fc2_scale) and, for fp8 storage, the fp8 codes are folded
-into bf16 copies of the weights once, outside the timed call, the way the reference's Lumen
-system pre-shuffles its weights (datasets/inference/moe/lumen/model.py:184-199) and its
-ksearch system caches dequantised weights (datasets/inference/moe/ksearch/main.cpp:23-37);
-fp8 activations are dequantised by a kernel inside every call.
+the python-backend contract (:339-403).
+
+fp8 input (the harness default): codes and block scales go to the kernels as they are; both
+expert GEMMs multiply fp8 on the tensor cores and apply the scales per 128-wide K block, the
+intermediate is re-quantised per row like the reference kernel does
+(datasets/inference/moe/lumen/fused_moe.py:400-443, 684-788).  Needs hidden and intermediate sizes
+that are multiples of 128 (the harness requires that too).  By default this route serves the
+token counts at which the expert GEMMs stream weights (up to 64 rows per expert); above that,
+and always with LUMEN_B200_MOE_FP8=dequant, codes and scales are folded into bf16 copies of the
+weights once, outside the timed call, the activations are dequantised in every call and the
+GEMMs compute in bf16.  LUMEN_B200_MOE_FP8=mma forces the fp8 kernels at every size.
+
+bf16 input: the expert GEMMs compute in bf16; non-unit block scales are folded into bf16 copies
+of the weights once, outside the timed call, the way the reference's Lumen system pre-shuffles
+its weights (datasets/inference/moe/lumen/model.py:184-199).
 """
 from __future__ import annotations
 
@@ -49,6 +58,22 @@ _pkg = _loader.load_b200_package()
 _moe = _pkg.moe
 
 BLOCK = 128
+
+
+FP8_KERNEL_ROWS = 64  # rows per expert up to which the fp8 kernels are the faster route
+
+
+def _use_fp8_kernels(tokens: int, topk: int, experts: int) -> bool:
+    """LUMEN_B200_MOE_FP8 = "mma": always the fp8 tensor-core kernels; "dequant": never; unset:
+    the fp8 kernels while the expert GEMMs stream weights (few rows per expert, where half the
+    bytes is close to half the time), the bf16 route above that (its 128 x 256 tiles have the
+    higher tensor-core rate; the fp8 kernels promote partial sums on CUDA cores per K block)."""
+    mode = os.environ.get("LUMEN_B200_MOE_FP8", "")
+    if mode == "mma":
+        return True
+    if mode == "dequant":
+        return False
+    return tokens * topk <= FP8_KERNEL_ROWS * experts
 
 
 def _tensor_key(t: torch.Tensor) -> tuple:
@@ -115,6 +140,26 @@ class Model:
             self._weight_key = key
         return self._weights
 
+    def _fp8_case(self, x, w, seq_len, dim, inter_dim, experts, topk) -> Callable[[], torch.Tensor]:
+        """fp8 codes and block scales straight into the fp8 kernels."""
+        dev = x.input_q.device
+        key = ("fp8", seq_len, dim, inter_dim, experts, topk, dev)
+        op = self._ops.get(key)
+        if op is None:
+            op = _moe.FusedMoEFp8(tokens=seq_len, hidden=dim, inter=inter_dim, experts=experts, topk=topk, device=dev)
+            self._ops[key] = op
+        self._out_cache[key] = op.out
+        xq, xscale = x.input_q.contiguous(), x.input_scale.to(torch.float32).contiguous()
+        ids = x.topk_ids.to(torch.int32).contiguous()
+        wts = x.topk_weights.to(torch.float32).contiguous()
+        w1q, w2q = w["w1_q"].contiguous(), w["w2_q"].contiguous()
+        s1, s2 = w["fc1_scale"].to(torch.float32).contiguous(), w["fc2_scale"].to(torch.float32).contiguous()
+
+        def run_b200_fp8() -> torch.Tensor:
+            return op.forward_routed(xq, xscale, ids, wts, w1q, s1, w2q, s2)
+
+        return run_b200_fp8
+
     def build_cases(self, *, seq_len: int, shared_input: Any, shared_weights: dict[str, torch.Tensor],
                     dim: int, inter_dim: int, experts: int, topk: int,
                     input_dtype: str) -> List[Callable[[], torch.Tensor]]:
@@ -128,10 +173,14 @@ class Model:
             raise ValueError(f"input_q shape mismatch: expected {(seq_len, dim)}, got {tuple(x.input_q.shape)}")
         if tuple(x.topk_ids.shape) != (seq_len, topk):
             raise ValueError(f"topk_ids shape mismatch: expected {(seq_len, topk)}, got {tuple(x.topk_ids.shape)}")
-        w13, w2 = self._prepare_weights(shared_weights)
-        if tuple(w13.shape) != (experts, inter_dim * 2, dim):
-            raise ValueError(f"w1_q shape mismatch: expected {(experts, inter_dim * 2, dim)}, got {tuple(w13.shape)}")
+        if tuple(shared_weights["w1_q"].shape) != (experts, inter_dim * 2, dim):
+            raise ValueError(f"w1_q shape mismatch: expected {(experts, inter_dim * 2, dim)}, "
+                             f"got {tuple(shared_weights['w1_q'].shape)}")
         fp8_in = x.input_q.dtype != torch.bfloat16
+        if fp8_in and shared_weights["w1_q"].dtype == x.input_q.dtype and dim % BLOCK == 0 \
+                and inter_dim % BLOCK == 0 and _use_fp8_kernels(seq_len, topk, experts):
+            return [self._fp8_case(x, shared_weights, seq_len, dim, inter_dim, experts, topk)]
+        w13, w2 = self._prepare_weights(shared_weights)
         # fp8 activations are dequantised by a kernel inside the timed call (they arrive as
         # fp8); bf16 activations with non-unit scales are scaled inside the call as well
         # (device arithmetic only), so that the closure always reads the caller's tensor

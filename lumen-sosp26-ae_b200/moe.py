@@ -388,3 +388,106 @@ class FusedMoE:
             for name, (e0, e1) in ev.items():
                 samples.setdefault(name, []).append(e0.elapsed_time(e1))
         return {name: statistics.median(v) for name, v in samples.items()}
+
+
+# --------------------------------------------------------------------------- fp8 block scale
+FP8_BLOCK = 128
+
+
+def fp8_code_factor(dtype: torch.dtype) -> float:
+    """What one unit of an fp8 code of `dtype` is worth relative to the same bits read as OCP
+    e4m3 (the tensor cores' format): 1 for float8_e4m3fn, 0.5 for float8_e4m3fnuz (exponent
+    bias 8 instead of 7; every finite code of one is a finite code of the other except the
+    fnuz values +-240, bit patterns 0x7F / 0xFF, which e4m3fn reads as NaN)."""
+    if dtype == torch.float8_e4m3fn:
+        return 1.0
+    if dtype == getattr(torch, "float8_e4m3fnuz", None):
+        return 0.5
+    raise ValueError(f"fp8 MoE takes float8_e4m3fn or float8_e4m3fnuz codes, got {dtype}")
+
+
+def gather_scales_t(scale: torch.Tensor, routes: SortedRoutes, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[T, KB] per-token block scales -> [KB, P] in expert order (1 for pad rows)."""
+    dev = _need_cuda(scale)
+    if scale.dtype != torch.float32 or scale.ndim != 2:
+        raise ValueError("scale must be a float32 [T, KB] tensor")
+    T, KB = scale.shape
+    P = routes.sorted_token_ids.numel()
+    if out is None:
+        out = torch.empty((KB, P), dtype=torch.float32, device=dev)
+    with _cabi.on_device(dev):
+        rc = _cabi.load().lumen_b200_moe_gather_scales_t(
+            scale.data_ptr(), routes.sorted_token_ids.data_ptr(), routes.num_valid_ids.data_ptr(),
+            out.data_ptr(), T, KB, P, _stream(dev))
+    _cabi.check("lumen_b200_moe_gather_scales_t", rc)
+    return out
+
+
+def grouped_gemm_fp8(acts_q: torch.Tensor, act_scale_t: torch.Tensor, weights_q: torch.Tensor,
+                     w_scale: torch.Tensor, routes, *, gated: bool, quantize_out: bool = False,
+                     scale_mul: float = 1.0, rows_hint: int = 0, out: torch.Tensor | None = None,
+                     out_scale_t: torch.Tensor | None = None):
+    """Per-expert fp8 block-scale GEMM (see lumen_b200_moe_grouped_gemm_fp8).  Returns `out`, or
+    (`out` codes as uint8, `out_scale_t`) when quantize_out."""
+    dev = _need_cuda(acts_q, act_scale_t, weights_q, w_scale)
+    if acts_q.element_size() != 1 or weights_q.element_size() != 1:
+        raise ValueError("acts_q and weights_q hold one-byte fp8 codes")
+    P, K = acts_q.shape
+    E, w_rows, K2 = weights_q.shape
+    N = w_rows // 2 if gated else w_rows
+    if K2 != K or K % FP8_BLOCK or N % FP8_BLOCK:
+        raise ValueError(f"K ({K}, {K2}) and N ({N}) must agree and be multiples of {FP8_BLOCK}")
+    if tuple(act_scale_t.shape) != (K // FP8_BLOCK, P) or act_scale_t.dtype != torch.float32:
+        raise ValueError(f"act_scale_t must be float32 [{K // FP8_BLOCK}, {P}]")
+    if w_scale.dtype != torch.float32 or w_scale.numel() != E * (w_rows // FP8_BLOCK) * (K // FP8_BLOCK):
+        raise ValueError("w_scale must be float32 [E, w_rows/128, K/128]")
+    if out is None:
+        out = torch.empty((P, N), dtype=torch.uint8 if quantize_out else torch.bfloat16, device=dev)
+    if quantize_out and out_scale_t is None:
+        out_scale_t = torch.ones((N // FP8_BLOCK, P), dtype=torch.float32, device=dev)
+    with _cabi.on_device(dev):
+        rc = _cabi.load().lumen_b200_moe_grouped_gemm_fp8(
+            acts_q.data_ptr(), act_scale_t.data_ptr(), weights_q.data_ptr(), w_scale.data_ptr(), out.data_ptr(),
+            out_scale_t.data_ptr() if quantize_out else None, routes.expert_offsets.data_ptr(),
+            routes.expert_counts.data_ptr(), P, E, N, K, 1 if gated else 0, 1 if quantize_out else 0,
+            float(scale_mul), int(rows_hint), _stream(dev))
+    _cabi.check("lumen_b200_moe_grouped_gemm_fp8", rc)
+    return (out, out_scale_t) if quantize_out else out
+
+
+class FusedMoEFp8:
+    """The MoE forward on fp8 codes and block scales, the reference harness' own format
+    (scripts/benchmark/backend_moe.py:86-210): sort -> gather codes and scales -> gated expert
+    GEMM in fp8 with the intermediate re-quantised per row and 128-column block -> second expert
+    GEMM in fp8 -> weighted combine.  No tensor is dequantised to bf16 on the way in."""
+
+    def __init__(self, *, tokens: int, hidden: int, inter: int, experts: int, topk: int, device: torch.device):
+        if hidden % FP8_BLOCK or inter % FP8_BLOCK:
+            raise ValueError(f"hidden ({hidden}) and inter ({inter}) must be multiples of {FP8_BLOCK}")
+        self.T, self.H, self.I, self.E, self.k = tokens, hidden, inter, experts, topk
+        self.device = device
+        P = max_padded_routes(tokens, topk, experts)
+        self.routes = alloc_sorted_routes(tokens, topk, experts, device)
+        need = int(_cabi.load().lumen_b200_moe_sort_scratch_bytes(tokens, experts, topk))
+        self.scratch = torch.empty((max(need, 4),), dtype=torch.uint8, device=device)
+        self.xs_q = torch.zeros((P, hidden), dtype=torch.uint8, device=device)
+        self.xs_scale_t = torch.ones((hidden // FP8_BLOCK, P), dtype=torch.float32, device=device)
+        self.h_q = torch.zeros((P, inter), dtype=torch.uint8, device=device)
+        self.h_scale_t = torch.ones((inter // FP8_BLOCK, P), dtype=torch.float32, device=device)
+        self.y = torch.empty((P, hidden), dtype=torch.bfloat16, device=device)
+        self.out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=device)
+        self.rows_hint = max(1, (tokens * topk + experts - 1) // experts)
+
+    def forward_routed(self, x_q, x_scale, topk_ids, topk_weights, w13_q, w13_scale, w2_q, w2_scale):
+        fx, f1, f2 = fp8_code_factor(x_q.dtype), fp8_code_factor(w13_q.dtype), fp8_code_factor(w2_q.dtype)
+        build_sorted_routes(topk_ids=topk_ids, topk_weights=topk_weights, experts=self.E,
+                            out=self.routes, scratch=self.scratch)
+        # a row of H one-byte codes moves as H / 2 two-byte elements
+        permute_rows(x_q.view(torch.uint8).view(torch.bfloat16), self.routes, out=self.xs_q.view(torch.bfloat16))
+        gather_scales_t(x_scale, self.routes, out=self.xs_scale_t)
+        grouped_gemm_fp8(self.xs_q, self.xs_scale_t, w13_q.view(torch.uint8), w13_scale, self.routes, gated=True,
+                         quantize_out=True, scale_mul=fx * f1, rows_hint=self.rows_hint, out=self.h_q,
+                         out_scale_t=self.h_scale_t)
+        grouped_gemm_fp8(self.h_q, self.h_scale_t, w2_q.view(torch.uint8), w2_scale, self.routes, gated=False,
+                         scale_mul=f2, rows_hint=self.rows_hint, out=self.y)
+        return combine(self.y, self.routes, topk_weights, self.T, out=self.out)

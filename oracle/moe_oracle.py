@@ -120,3 +120,71 @@ def moe_inputs(tokens: int, hidden: int, inter: int, experts: int, seed: int, *,
     w2 = (torch.randn((experts, hidden, inter), generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
     w13 = torch.cat([w1, w3], dim=1).to(torch.bfloat16)
     return dict(x=x, logits=logits, w_router=w_router, w13=w13, w2=w2)
+
+
+BLOCK = 128  # scale block edge (scripts/benchmark/backend_moe.py:19-20)
+
+
+def block_dequant(codes: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """codes [rows, cols] (any dtype, read by value) times scale [(rows/128) * (cols/128)] ->
+    fp32: `_dequantize_weight` (scripts/benchmark/backend_moe.py:507-525)."""
+    rows, cols = codes.shape
+    s = scale.to(torch.float32).reshape(rows // BLOCK, 1, cols // BLOCK, 1)
+    return (codes.to(torch.float32).reshape(rows // BLOCK, BLOCK, cols // BLOCK, BLOCK) * s).reshape(rows, cols)
+
+
+def quantize_rows_e4m3(h: torch.Tensor):
+    """Per row and 128-column block: scale = max|h| / 448 (1 for an all-zero block), codes =
+    e4m3fn(h / scale).  Returns (dequantised h, scales [rows, cols/128]).  Models the per-row
+    re-quantisation of the intermediate (datasets/inference/moe/lumen/fused_moe.py:684-788) with
+    the OCP e4m3 range of the target hardware."""
+    rows, cols = h.shape
+    hb = h.to(torch.float32).reshape(rows, cols // BLOCK, BLOCK)
+    amax = hb.abs().amax(dim=-1, keepdim=True)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (hb / scale).to(torch.float8_e4m3fn).to(torch.float32)
+    return (q * scale).reshape(rows, cols), scale.squeeze(-1)
+
+
+def moe_reference_blockscale(x_q, x_scale, w13_q, w13_scale, w2_q, w2_scale, topk_ids, topk_weights, *,
+                             quantize_h: bool = False) -> torch.Tensor:
+    """`_moe_reference` (scripts/benchmark/backend_moe.py:469-504) with its block scales: x_q [T,H]
+    and the weights are fp8 (or bf16) codes read by value, x_scale [T,H/128], w13_scale
+    [E,(2I/128)*(H/128)], w2_scale [E,(H/128)*(I/128)].  fp32 throughout, bf16 out.
+    quantize_h=True re-quantises the intermediate like the fp8 kernels do."""
+    T, H = x_q.shape
+    E, two_i, _ = w13_q.shape
+    inter = two_i // 2
+    xf = (x_q.to(torch.float32).reshape(T, H // BLOCK, BLOCK) * x_scale.to(torch.float32).unsqueeze(-1)).reshape(T, H)
+    out = torch.zeros((T, H), dtype=torch.float32)
+    for e in range(E):
+        tok, slot = torch.nonzero(topk_ids == e, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        stage1 = xf[tok] @ block_dequant(w13_q[e], w13_scale[e]).transpose(0, 1)
+        gate, up = stage1.split(inter, dim=-1)
+        h = F.silu(gate) * up
+        if quantize_h:
+            h, _ = quantize_rows_e4m3(h)
+        expert_out = h @ block_dequant(w2_q[e], w2_scale[e]).transpose(0, 1)
+        out.index_add_(0, tok, expert_out * topk_weights[tok, slot].unsqueeze(1))
+    return out.to(torch.bfloat16)
+
+
+def moe_fp8_inputs(tokens: int, hidden: int, inter: int, experts: int, topk: int, seed: int,
+                   dtype=torch.float8_e4m3fn, w_scale: float = 1e-2):
+    """Seeded stand-ins with the distributions of the harness' fp8 mode
+    (scripts/benchmark/backend_moe.py:86-210): x = randn + 0.1 and weights = randn * 8 cast to fp8,
+    positive block scales around 0.1 (activations) and `w_scale` (weights; the harness uses 0.01,
+    the parity tests a larger value so that outputs are of order 1), routing from N(0,1) scores."""
+    g = torch.Generator().manual_seed(seed)
+    x_q = (torch.randn((tokens, hidden), generator=g) + 0.1).to(dtype)
+    x_scale = (torch.randn((tokens, hidden // BLOCK), generator=g) * 2e-2 + 1e-1).clamp_min(1e-8)
+    ids, weights = route_topk(torch.randn((tokens, experts), generator=g), topk)
+    gw = torch.Generator().manual_seed(seed + 17)
+    w13_q = (torch.randn((experts, 2 * inter, hidden), generator=gw) * 8.0).to(dtype)
+    w2_q = (torch.randn((experts, hidden, inter), generator=gw) * 8.0).to(dtype)
+    w13_scale = (torch.randn((experts, (2 * inter // BLOCK) * (hidden // BLOCK)), generator=gw) * 0.2 * w_scale + w_scale).clamp_min(1e-8)
+    w2_scale = (torch.randn((experts, (hidden // BLOCK) * (inter // BLOCK)), generator=gw) * 0.2 * w_scale + w_scale).clamp_min(1e-8)
+    return dict(x_q=x_q, x_scale=x_scale, topk_ids=ids, topk_weights=weights, w13_q=w13_q, w13_scale=w13_scale,
+                w2_q=w2_q, w2_scale=w2_scale)

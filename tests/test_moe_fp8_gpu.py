@@ -1,0 +1,112 @@
+"""GPU parity of the fp8 block-scale MoE path (tcgen05.mma.kind::f8f6f4 with per-128-K-block
+scale promotion) against the CPU oracle, through the C-ABI.
+
+The oracle dequantises codes by value and computes in fp32 (the reference's `_moe_reference`,
+scripts/benchmark/backend_moe.py:469-525).  The kernels re-quantise the gated intermediate to fp8
+per row and 128-column block, as the reference kernel does; the oracle can model that step
+(quantize_h=True), which is the tight comparison, and without it the comparison uses the
+reference harness' own tolerance for this operator (1e-1, scripts/benchmark/backend_moe.py:22-25).
+The test inputs use larger weight scales than the harness so that outputs are of order 10 rather
+than 0.03 (where any absolute tolerance is vacuous); absolute allowances are therefore taken
+relative to the outputs' RMS.  The harness' own distributions and check run in
+tests/test_harness_gpu.py (bench_moe --input-dtype fp8 --check-correctness).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ATOL, RTOL
+from oracle import moe_oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+FNUZ = getattr(torch, "float8_e4m3fnuz", None)
+
+
+def _routes(pkg, d, E):
+    return pkg.moe.build_sorted_routes(topk_ids=d["topk_ids"].to(DEV), topk_weights=d["topk_weights"].to(DEV), experts=E)
+
+
+@pytest.mark.parametrize("T,H,I,E,k", [(300, 512, 256, 8, 2), (1, 256, 128, 4, 2), (130, 384, 384, 4, 4)])
+def test_expert_gemms_match_dequantised_fp32(cuda_pkg, T, H, I, E, k):
+    """Each of the two expert GEMMs on its own: codes gathered into expert order, scales gathered
+    K-block-major, product against the fp32 matmul of the dequantised operands."""
+    moe = cuda_pkg.moe
+    d = moe_oracle.moe_fp8_inputs(T, H, I, E, k, seed=7 + T, w_scale=8e-2)
+    r = _routes(cuda_pkg, d, E)
+    P = r.sorted_token_ids.numel()
+    xs_q = torch.zeros((P, H), dtype=torch.uint8, device=DEV)
+    moe.permute_rows(d["x_q"].to(DEV).view(torch.uint8).view(torch.bfloat16), r, out=xs_q.view(torch.bfloat16))
+    xs_scale_t = moe.gather_scales_t(d["x_scale"].to(DEV), r)
+    torch.cuda.synchronize()
+    tok = (r.sorted_token_ids.cpu() & 0xFFFFFF).long()
+    valid = tok < T
+    # the gathered scales: [KB, P], 1 for pad rows
+    want_scale = torch.ones((H // 128, P))
+    want_scale[:, valid] = d["x_scale"][tok[valid]].T
+    assert torch.equal(xs_scale_t.cpu(), want_scale)
+    xf = torch.zeros((P, H))
+    xf[valid] = (d["x_q"].float().reshape(T, H // 128, 128) * d["x_scale"].unsqueeze(-1)).reshape(T, H)[tok[valid]]
+
+    offs, cnts = r.expert_offsets.cpu().numpy(), r.expert_counts.cpu().numpy()
+    # first GEMM, gated, bf16 out (no re-quantisation): silu(x W1^T) * (x W3^T)
+    h = moe.grouped_gemm_fp8(xs_q, xs_scale_t, d["w13_q"].to(DEV).view(torch.uint8), d["w13_scale"].to(DEV), r,
+                             gated=True)
+    # and with re-quantisation: codes * scales must equal the oracle's quantised intermediate
+    h_q, h_scale_t = moe.grouped_gemm_fp8(xs_q, xs_scale_t, d["w13_q"].to(DEV).view(torch.uint8),
+                                          d["w13_scale"].to(DEV), r, gated=True, quantize_out=True)
+    y = moe.grouped_gemm_fp8(h_q, h_scale_t, d["w2_q"].to(DEV).view(torch.uint8), d["w2_scale"].to(DEV), r,
+                             gated=False)
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    h_deq = (h_q.cpu().view(torch.float8_e4m3fn).float().reshape(P, I // 128, 128)
+             * h_scale_t.cpu().T.unsqueeze(-1)).reshape(P, I)
+    for e in range(E):
+        a, n = int(offs[e]), int(cnts[e])
+        if n == 0:
+            continue
+        s1 = xf[a:a + n] @ moe_oracle.block_dequant(d["w13_q"][e], d["w13_scale"][e]).T
+        want_h = torch.nn.functional.silu(s1[:, :I]) * s1[:, I:]
+        torch.testing.assert_close(h[a:a + n].cpu().float(), want_h, rtol=RTOL, atol=ATOL)
+        want_hq, want_hs = moe_oracle.quantize_rows_e4m3(want_h)
+        # scales to fp32 rounding; codes may differ by one e4m3 step where h/scale sits on a tie
+        torch.testing.assert_close(h_scale_t.cpu().T[a:a + n], want_hs, rtol=1e-3, atol=1e-6)
+        torch.testing.assert_close(h_deq[a:a + n], want_hq, rtol=0.13, atol=want_hs.max().item() * 2)
+        # second GEMM on the kernel's own quantised intermediate
+        want_y = h_deq[a:a + n] @ moe_oracle.block_dequant(d["w2_q"][e], d["w2_scale"][e]).T
+        torch.testing.assert_close(y[a:a + n].cpu().float(), want_y, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("dtype", [torch.float8_e4m3fn, FNUZ])
+@pytest.mark.parametrize("T,H,I,E,k", [(300, 512, 256, 8, 2), (64, 1024, 512, 32, 8), (1, 256, 128, 4, 2),
+                                       (700, 256, 384, 4, 2)])
+def test_forward_matches_oracle(cuda_pkg, dtype, T, H, I, E, k):
+    if dtype is None:
+        pytest.skip("this torch build has no float8_e4m3fnuz")
+    d = moe_oracle.moe_fp8_inputs(T, H, I, E, k, seed=20260319 + T, dtype=dtype, w_scale=8e-2)
+    op = cuda_pkg.moe.FusedMoEFp8(tokens=T, hidden=H, inter=I, experts=E, topk=k, device=DEV)
+    g = {key: v.to(DEV) for key, v in d.items()}
+    out = op.forward_routed(g["x_q"], g["x_scale"], g["topk_ids"], g["topk_weights"], g["w13_q"], g["w13_scale"],
+                            g["w2_q"], g["w2_scale"])
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    args = (d["x_q"], d["x_scale"], d["w13_q"], d["w13_scale"], d["w2_q"], d["w2_scale"], d["topk_ids"],
+            d["topk_weights"])
+    tight = moe_oracle.moe_reference_blockscale(*args, quantize_h=True)
+    # Outputs are of order 10 here.  Where an intermediate value sits on a rounding tie of the
+    # 3-bit e4m3 mantissa, kernel and oracle may pick neighbouring codes (one step = 6-12 % of
+    # that one value), so the absolute allowance is 2 % of the outputs' RMS, not of 1.
+    rms = float(tight.float().pow(2).mean().sqrt())
+    torch.testing.assert_close(out.cpu().float(), tight.float(), rtol=RTOL, atol=ATOL * max(1.0, rms))
+    loose = moe_oracle.moe_reference_blockscale(*args, quantize_h=False)
+    torch.testing.assert_close(out.cpu().float(), loose.float(), rtol=1e-1, atol=1e-1 * max(1.0, rms))
+
+
+def test_shapes_that_do_not_fill_scale_blocks_are_refused(cuda_pkg):
+    moe = cuda_pkg.moe
+    with pytest.raises(ValueError, match="multiples of 128"):
+        moe.FusedMoEFp8(tokens=8, hidden=192, inter=128, experts=2, topk=1, device=DEV)
+    with pytest.raises(ValueError, match="e4m3"):
+        moe.fp8_code_factor(torch.float16)
