@@ -716,6 +716,24 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
+// One row of `chunks` 16-byte pieces by a whole CTA: four loads in flight per thread before the
+// (possibly remote) stores, so that a row does not cost a load latency per piece.
+__device__ __forceinline__ void copy_row_16b(uint4* __restrict__ dst, const uint4* __restrict__ src, int chunks) {
+  for (int c0 = threadIdx.x; c0 < chunks; c0 += 4 * blockDim.x) {
+    uint4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = c0 + i * blockDim.x;
+      if (c < chunks) v[i] = __ldg(src + c);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = c0 + i * blockDim.x;
+      if (c < chunks) dst[c] = v[i];
+    }
+  }
+}
+
 // Dispatch: for every compactly sorted route of this GPU, copy the token's row into the
 // owner GPU's grouped buffer.  One CTA per route (grid-stride), 16-byte copies.
 __global__ void __launch_bounds__(256)
@@ -737,7 +755,7 @@ __global__ void __launch_bounds__(256)
     }
     uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peers.p[e / El]) + size_t(dst_row) * H);
     const uint4* src = reinterpret_cast<const uint4*>(x + size_t(token) * H);
-    for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+    copy_row_16b(dst, src, chunks);
   }
   __threadfence_system();
 }
@@ -767,7 +785,7 @@ __global__ void __launch_bounds__(256)
     }
     uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peers.p[src_gpu]) + size_t(dst_row) * H);
     const uint4* src = reinterpret_cast<const uint4*>(y + size_t(g) * H);
-    for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+    copy_row_16b(dst, src, chunks);
   }
   __threadfence_system();
 }
