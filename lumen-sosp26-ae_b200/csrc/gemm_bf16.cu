@@ -52,10 +52,41 @@ int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& ar
   return launch_overlapped(kern, dim3(grid), dim3(kGemmThreads), smem, st, mp, mq, args);
 }
 
-// dense GEMM on CTA pairs (clusters of 2); grid = 2 CTAs per co-resident cluster
+constexpr int kSplitCounterSlots = 4096;  // split-K arrival counters at the head of a workspace
+
+// Split of the last, partial wave of a CTA-pair launch: the `units % pairs` tiles left over
+// after the full rounds are cut into `slices` K slices each, one slice per pair.
+struct PairTailPlan {
+  int slices;      // 1 = no split
+  int tail_first;  // first split tile
+  size_t bytes;    // fp32 partial tiles
+};
+
+PairTailPlan plan_pair_tail(int units, int pairs, int K, int bn) {
+  PairTailPlan p{1, units, 0};
+  static const bool enabled = [] {
+    const char* v = std::getenv("LUMEN_B200_GEMM_TAIL");  // "0" switches the split off
+    return !(v && v[0] == '0');
+  }();
+  if (!enabled || pairs <= 0 || units <= 0) return p;
+  const int rem = units % pairs;
+  if (rem == 0) return p;
+  const int k_blocks = (K + kBlockK - 1) / kBlockK;
+  int slices = pairs / rem;
+  if (slices > k_blocks / 8) slices = k_blocks / 8;  // at least 8 K blocks per slice
+  slices = slices >= 8 ? 8 : slices >= 4 ? 4 : slices >= 2 ? 2 : 1;  // a divisor of the tile's 32-column chunks
+  if (slices < 2) return p;
+  p.slices = slices;
+  p.tail_first = units - rem;
+  p.bytes = size_t(rem) * slices * kPairTileM * bn * sizeof(float);
+  return p;
+}
+
+// dense GEMM on CTA pairs (clusters of 2); grid = 2 CTAs per co-resident cluster.  With a
+// workspace that is large enough, the last partial wave is split along K.
 template <int STAGES, int BN>
-int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int units,
-                     cudaStream_t st) {
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args_in, int units,
+                     void* workspace, size_t workspace_bytes, cudaStream_t st) {
   auto kern = gemm_bf16_pair_kernel<STAGES, BN>;
   constexpr size_t smem = gemm_pair_smem_bytes<STAGES, BN>();
   static_assert(smem <= 227 * 1024, "stage ring does not fit shared memory");
@@ -79,7 +110,22 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
     max_clusters[dev] = n;
     configured[dev] = true;
   }
-  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  GemmArgs args = args_in;
+  args.splits = 1;
+  args.tail_first = units;
+  int work = units;
+  const PairTailPlan plan = plan_pair_tail(units, max_clusters[dev], args.K, BN);
+  constexpr size_t counter_bytes = size_t(kSplitCounterSlots) * sizeof(int);
+  if (plan.slices > 1 && workspace && workspace_bytes >= counter_bytes + plan.bytes) {
+    // the arrival counters at the head of the workspace are zero on entry (the caller zero-fills
+    // a new workspace once) and the kernel leaves them zero
+    args.splits = plan.slices;
+    args.tail_first = plan.tail_first;
+    args.counters = static_cast<int*>(workspace);
+    args.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + counter_bytes);
+    work = plan.tail_first + (units - plan.tail_first) * plan.slices;
+  }
+  const int clusters = work < max_clusters[dev] ? work : max_clusters[dev];
   return launch_overlapped(kern, dim3(2 * clusters), dim3(kGemmThreads), smem, st, ma, mb, args);
 }
 
@@ -156,7 +202,6 @@ int forced_pair_tile_n() {
 
 inline int ceil_div_h(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
-constexpr int kSplitCounterSlots = 4096;  // output tiles a split-K launch may have
 
 // swapped dense path: tile geometry and split-K plan for M <= 128
 struct SwapPlan {
@@ -208,7 +253,14 @@ extern "C" size_t lumen_b200_gemm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int sms = device_sm_count();
   if (sms <= 0) return 0;
-  if (!takes_streaming_path(M, N, K, sms)) return 0;
+  if (!takes_streaming_path(M, N, K, sms)) {
+    if (!use_pair_tiles()) return 0;
+    // CTA pairs: room for the K slices of the last partial wave, if this shape has one to split
+    const int bn = forced_pair_tile_n() ? forced_pair_tile_n() : pick_pair_tile_n(M, N, sms / 2);
+    const int units = ((M + kPairTileM - 1) / kPairTileM) * ((N + bn - 1) / bn);
+    const PairTailPlan tail = plan_pair_tail(units, sms / 2, K, bn);
+    return tail.slices > 1 ? size_t(kSplitCounterSlots) * sizeof(int) + tail.bytes : 0;
+  }
   const SwapPlan p = plan_swap(M, N, K, sms);
   return p.splits > 1 ? p.counter_bytes + p.partial_bytes : 0;
 }
@@ -243,8 +295,8 @@ extern "C" int lumen_b200_gemm_bf16_nt(const void* A, const void* B, void* C, in
     if (encode_tmap_bf16_2d(&mp, A, M, K, lda, kBlockP) != 0) return LUMEN_B200_ECUDA;
     if (encode_tmap_bf16_2d(&mq, B, N, K, ldb, bn / 2) != 0) return LUMEN_B200_ECUDA;
     const int units = ((M + kPairTileM - 1) / kPairTileM) * ((N + bn - 1) / bn);
-    return bn == 128 ? launch_gemm_pair<8, 128>(mp, mq, args, units, st)
-                     : launch_gemm_pair<6, 256>(mp, mq, args, units, st);
+    return bn == 128 ? launch_gemm_pair<8, 128>(mp, mq, args, units, workspace, workspace_bytes, st)
+                     : launch_gemm_pair<6, 256>(mp, mq, args, units, workspace, workspace_bytes, st);
   }
   if (!streaming) {
     // P = A (128-row boxes), Q = B (256-row boxes)

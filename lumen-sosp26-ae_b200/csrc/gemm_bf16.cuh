@@ -35,6 +35,7 @@ enum GemmWaitCode {
   kWaitFullStage = 2,
   kWaitTmemEmpty = 3,
   kWaitTmemFull = 4,
+  kWaitSlices = 5,  // CTA pairs: the other K slices of a split tile did not arrive
 };
 
 struct GemmArgs {
@@ -43,9 +44,10 @@ struct GemmArgs {
   int M;  // activation rows (dense) / unused (grouped)
   int N;  // output columns = weight rows per expert that produce outputs
   int K;
-  int splits;     // split-K factor (swapped dense only; 1 otherwise)
+  int splits;     // split-K factor: K slices per tile (swapped dense) or per tile of the last, partial wave (CTA pairs); 1 = none
+  int tail_first; // CTA pairs: first output tile that is split over K (tiles before it run whole)
   float* ws;      // split-K partial tiles
-  int* counters;  // split-K arrival counters, one per output tile, zero between launches
+  int* counters;  // split-K arrival counters, zero between launches
   // grouped
   const int* expert_offsets;  // [E+1] first activation row of each expert
   const int* expert_counts;   // [E] valid rows of each expert

@@ -9,6 +9,14 @@
 // "full" barrier, the leader's single MMA thread issues for the pair and its commits
 // arrive on the barriers of both CTAs.
 //
+// Tail of the last wave.  A launch runs its tiles round-robin over the CTA pairs, so the last
+// round keeps only (tiles mod pairs) of them busy.  When that remainder R is at most half
+// of the pairs, each of the last R tiles is cut into s = pairs / R slices along K (at least
+// 8 K blocks each; s = 2, 4 or 8), one slice per pair: the last round then takes 1 / s of a full
+// one.  The slices of a tile exchange fp32 partial sums through the workspace like a
+// reduce-scatter (each finishes 1 / s of the columns, adding in slice order, so the result is the
+// same from run to run).  Without a workspace the launcher does not split.
+//
 // Roles per CTA as in gemm_bf16.cuh: warp 0 TMA producer, warp 1 TMEM allocator (+ MMA
 // issuer in the leader), warps 2..5 epilogue of this CTA's 128 rows.
 #pragma once
@@ -57,6 +65,39 @@ __device__ __forceinline__ PairUnit pair_decode(int u, int tiles_m, int tiles_n)
   const int nt = r / gsz;
   const int mt = g * kGroup + (r - nt * gsz);
   return PairUnit{mt * kPairTileM, nt * BN};
+}
+
+// One piece of work of a pair: an output tile over K blocks [kb0, kb1).
+struct PairWork {
+  int m0, n0;
+  int kb0, kb1;
+  int slice, slices;  // slices == 1: the whole K range, stored directly
+  int tail_idx;       // index of the tile among the split ones
+};
+
+template <int BN>
+__device__ __forceinline__ PairWork pair_work(int w, int tiles_m, int tiles_n, int k_blocks, int tail_first,
+                                              int slices) {
+  PairWork r;
+  int u = w;
+  r.kb0 = 0;
+  r.kb1 = k_blocks;
+  r.slice = 0;
+  r.slices = 1;
+  r.tail_idx = 0;
+  if (w >= tail_first) {
+    const int x = w - tail_first;
+    r.tail_idx = x / slices;
+    r.slice = x - r.tail_idx * slices;
+    r.slices = slices;
+    u = tail_first + r.tail_idx;
+    r.kb0 = (k_blocks * r.slice) / slices;
+    r.kb1 = (k_blocks * (r.slice + 1)) / slices;
+  }
+  const PairUnit t = pair_decode<BN>(u, tiles_m, tiles_n);
+  r.m0 = t.m0;
+  r.n0 = t.n0;
+  return r;
 }
 
 // BN = 256 or 128 output columns per tile (the narrower tile halves the unit of work, which
@@ -120,6 +161,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int k_blocks = ceil_div(args.K, kBlockK);
   const int pair_id = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
+  // pieces of work: whole tiles [0, tail_first), then `slices` K slices of each later tile
+  const int slices = args.splits > 1 ? args.splits : 1;
+  const int tail_first = slices > 1 ? args.tail_first : total_units;
+  const int total_work = tail_first + (total_units - tail_first) * slices;
 
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) ======================
@@ -127,11 +172,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = pair_id; u < total_units && ok; u += num_pairs) {
-        const PairUnit t = pair_decode<BN>(u, tiles_m, tiles_n);
+      for (int w = pair_id; w < total_work && ok; w += num_pairs) {
+        const PairWork t = pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
         const int a_row = t.m0 + int(rank) * kBlockP;
         const int b_row = t.n0 + int(rank) * (BN / 2);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = t.kb0; kb < t.kb1; ++kb) {
           if (!mbar_wait(smem_u32(&tail->empty[stage]), phase ^ 1u, ctx, kWaitEmptyStage)) {
             ok = false;
             break;
@@ -157,7 +202,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int u = pair_id; u < total_units && ok; u += num_pairs, ++it) {
+      for (int w = pair_id; w < total_work && ok; w += num_pairs, ++it) {
+        const PairWork t = pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
         const int buf = it & 1;
         const uint32_t buf_phase = (it >> 1) & 1;
         if (!mbar_wait(smem_u32(&tail->tmem_empty[buf]), buf_phase ^ 1u, ctx, kWaitTmemEmpty)) {
@@ -166,7 +212,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = t.kb0; kb < t.kb1; ++kb) {
           if (!mbar_wait(smem_u32(&tail->full[stage]), phase, ctx, kWaitFullStage)) {
             ok = false;
             break;
@@ -178,7 +224,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kBlockK / kUmmaK; ++k) {
             umma_bf16_ss_pair(d_tmem, make_smem_desc_sw128(sa + k * kUmmaK * 2, 0, 1024),
                               make_smem_desc_sw128(sb + k * kUmmaK * 2, 0, 1024), idesc,
-                              (kb > 0 || k > 0) ? 1u : 0u);
+                              (kb > t.kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(smem_u32(&tail->empty[stage]), 3);
           if (++stage == STAGES) {
@@ -196,8 +242,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const bool vec_ok = (args.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
     int it = 0;
     bool ok = true;
-    for (int u = pair_id; u < total_units && ok; u += num_pairs, ++it) {
-      const PairUnit t = pair_decode<BN>(u, tiles_m, tiles_n);
+    for (int w = pair_id; w < total_work && ok; w += num_pairs, ++it) {
+      const PairWork t = pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
       const int buf = it & 1;
       const uint32_t buf_phase = (it >> 1) & 1;
       if (!mbar_wait(smem_u32(&tail->tmem_full[buf]), buf_phase, ctx, kWaitTmemFull)) {
@@ -211,33 +257,125 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const bool row_ok = row < args.M;
       const int cols_valid = min(BN, args.N - t.n0);
       __nv_bfloat16* orow = args.out + size_t(row) * args.ldo + t.n0;
+      // 32 fp32 values of this thread's row, columns [c * 32, c * 32 + 32) of the tile -> bf16 -> C
+      auto store_chunk = [&](const uint32_t (&v)[32], int c) {
+        if (!row_ok) return;
+        const int col0 = c * 32;
+        if (vec_ok && col0 + 32 <= cols_valid) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 q;
+            q.x = pack_bf16x2(__uint_as_float(v[j + 0]), __uint_as_float(v[j + 1]));
+            q.y = pack_bf16x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+            q.z = pack_bf16x2(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
+            q.w = pack_bf16x2(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
+            *reinterpret_cast<uint4*>(orow + col0 + j) = q;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < cols_valid) orow[col0 + j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+        }
+      };
+      if (t.slices == 1) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_acc + c * 32, v);
+          tmem_ld_wait();
+          store_chunk(v, c);
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(smem_u32(&tail->tmem_empty[buf]), 0);
+        continue;
+      }
+      // ---- one K slice of a split tile ----
+      // The `slices` pairs that share the tile exchange partial sums through the workspace like
+      // a reduce-scatter: slice i finishes the 32-column chunks [i * own, (i + 1) * own) of every
+      // row, so it stores its other chunks, waits until the warps of the other slices that hold
+      // the same 32 rows have stored theirs, and adds what they left for its chunks, in slice
+      // order.  All pairs of a launch are resident together, so the wait is on running CTAs; it
+      // is bounded like every other wait.
+      // workspace: [tile][writing slice][CTA of the pair][128 rows][BN] fp32
+      constexpr int kChunks = BN / 32;
+      constexpr size_t kHalfTile = size_t(kBlockP) * BN;
+      const int own = kChunks / t.slices;
+      const int own_first = t.slice * own;
+      float* tile_ws = args.ws + size_t(t.tail_idx) * t.slices * 2 * kHalfTile;
+      float* mine = tile_ws + (size_t(t.slice) * 2 + rank) * kHalfTile + size_t(p) * BN;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        if (c >= own_first && c < own_first + own) continue;
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_acc + c * 32, v);
         tmem_ld_wait();
-        if (row_ok) {
-          const int col0 = c * 32;
-          if (vec_ok && col0 + 32 <= cols_valid) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 q;
-              q.x = pack_bf16x2(__uint_as_float(v[j + 0]), __uint_as_float(v[j + 1]));
-              q.y = pack_bf16x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-              q.z = pack_bf16x2(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
-              q.w = pack_bf16x2(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
-              *reinterpret_cast<uint4*>(orow + col0 + j) = q;
+        for (int j = 0; j < 32; j += 4)
+          __stcg(reinterpret_cast<uint4*>(mine + c * 32 + j), make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      }
+      __threadfence();
+      __syncwarp();
+      int* arrivals = args.counters + ((t.tail_idx * 2 + int(rank)) * 4 + quad) * 2;
+      int* departures = arrivals + 1;
+      int seen = 1;
+      if (lane == 0) {
+        atomicAdd(arrivals, 1);
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(arrivals) < t.slices) {
+          if ((++spins & 0xffu) == 0u) {
+            if (*ctx.cta_abort) {
+              seen = 0;
+              break;
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < cols_valid) orow[col0 + j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              *ctx.cta_abort = 1;
+              atomicCAS(ctx.status, 0, (kWaitSlices << 16) | static_cast<int>(blockIdx.x & 0xffffu));
+              seen = 0;
+              break;
+            }
           }
         }
       }
+      seen = __shfl_sync(0xffffffffu, seen, 0);
+      if (!seen) {
+        ok = false;
+        break;
+      }
+      __threadfence();
+      const float* rows = tile_ws + size_t(rank) * kHalfTile + size_t(p) * BN;
+#pragma unroll 1
+      for (int c = own_first; c < own_first + own; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_acc + c * 32, v);
+        tmem_ld_wait();
+        for (int sl = 0; sl < t.slices; ++sl) {
+          if (sl == t.slice) continue;
+          const float* src = rows + size_t(sl) * 2 * kHalfTile + c * 32;
+          uint4 x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = __ldcg(reinterpret_cast<const uint4*>(src) + j);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            v[4 * j + 0] = __float_as_uint(__uint_as_float(v[4 * j + 0]) + __uint_as_float(x[j].x));
+            v[4 * j + 1] = __float_as_uint(__uint_as_float(v[4 * j + 1]) + __uint_as_float(x[j].y));
+            v[4 * j + 2] = __float_as_uint(__uint_as_float(v[4 * j + 2]) + __uint_as_float(x[j].z));
+            v[4 * j + 3] = __float_as_uint(__uint_as_float(v[4 * j + 3]) + __uint_as_float(x[j].w));
+          }
+        }
+        store_chunk(v, c);
+      }
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(smem_u32(&tail->tmem_empty[buf]), 0);
+      if (lane == 0) {
+        mbar_arrive_cluster(smem_u32(&tail->tmem_empty[buf]), 0);
+        // the last of the slices to have read resets both counters for the next launch
+        if (atomicAdd(departures, 1) == t.slices - 1) {
+          *departures = 0;
+          *arrivals = 0;
+        }
+      }
     }
   }
 

@@ -54,6 +54,54 @@ def test_exact_on_integer_valued_inputs(cuda_pkg):
     assert torch.equal(out, gemm_oracle.gemm_reference(a[:9], b))
 
 
+# Shapes whose last round of 256 x 256 tiles fills at most half of the CTA pairs, so that its
+# tiles are computed as K slices and summed through the workspace (ragged edges included), and
+# one whose tile count divides evenly (no split).
+TAIL_SHAPES = [(1000, 6000, 2048), (1024, 6144, 4096), (2048, 2560, 1024), (4096, 4096, 1536), (2048, 9472, 512)]
+
+
+@pytest.mark.parametrize("m,n,k", TAIL_SHAPES)
+def test_split_last_wave_matches_oracle_rows(cuda_pkg, m, n, k):
+    dev = torch.device("cuda:0")
+    a, b = gemm_oracle.gemm_inputs(m, n, k, seed=20260312 + m + n + k)
+    ad, bd = a.to(dev), b.to(dev)
+    out = cuda_pkg.gemm_pipeline_transposed_b(ad, bd)
+    again = cuda_pkg.gemm_pipeline_transposed_b(ad, bd)
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    # the slices are added in slice order, whichever arrives last: bit-identical from run to run
+    assert torch.equal(out, again)
+    # every tile row and column band, the last (split) tiles included
+    rows = torch.unique(torch.cat([torch.arange(0, m, 37), torch.arange(max(0, m - 300), m, 7)]))
+    want = gemm_oracle.gemm_reference(a[rows], b)
+    torch.testing.assert_close(out[rows.to(dev)].cpu().float(), want.float(), rtol=RTOL, atol=ATOL)
+
+
+def test_split_last_wave_is_exact_on_integers_and_optional(cuda_pkg):
+    """Integer-valued operands: every partial sum is exact, so the split result equals the
+    oracle bit for bit; the same call without a workspace (no split) must agree."""
+    import ctypes
+
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(11)
+    m, n, k = 1024, 6144, 1024
+    a = torch.randint(-3, 4, (m, k), generator=g).to(torch.bfloat16)
+    b = torch.randint(-3, 4, (n, k), generator=g).to(torch.bfloat16)
+    ad, bd = a.to(dev), b.to(dev)
+    assert cuda_pkg.gemm_workspace_bytes(m, n, k) > 0  # this shape has a tail to split
+    out = cuda_pkg.gemm_pipeline_transposed_b(ad, bd)
+    plain = torch.empty_like(out)
+    lib = cuda_pkg._cabi.load()
+    rc = lib.lumen_b200_gemm_bf16_nt(ad.data_ptr(), bd.data_ptr(), plain.data_ptr(), m, n, k, k, k, n, None, 0,
+                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    want = gemm_oracle.gemm_reference(a[::5], b)
+    assert torch.equal(out.cpu()[::5], want)
+    assert torch.equal(out, plain)
+
+
 def test_caller_owned_output_and_pitch(cuda_pkg):
     dev = torch.device("cuda:0")
     a, b = gemm_oracle.gemm_inputs(200, 264, 128, seed=3)
