@@ -64,7 +64,11 @@ int lumen_b200_status_snapshot(int* host_dst, void* stream);
  * to nearest even.  Row-major with pitches lda, ldb, ldc in elements; lda and ldb
  * must be multiples of 8 and A, B 16-byte aligned.  M <= 128 (and problems too small
  * to fill the GPU with 256 x 256 tiles) take the weight-streaming split-K path, which
- * uses `workspace`; with workspace == NULL that path runs unsplit.  A new workspace must be zero-filled once by the caller;
+ * uses `workspace`; with workspace == NULL that path runs unsplit.  Larger problems use the
+ * workspace only to split the tiles of their last, partial wave over the idle SMs: with
+ * workspace == NULL, or one smaller than lumen_b200_gemm_workspace_bytes(), they run
+ * unsplit with the same result up to fp32 summation order.  A new workspace must be
+ * zero-filled once by the caller;
  * every call leaves its first lumen_b200_gemm_workspace_bytes() bytes reusable by the
  * next call on the same stream (calls that overlap on the GPU need separate workspaces).
  * Replaces gemm_pipeline_transposed_b(A, B, out)

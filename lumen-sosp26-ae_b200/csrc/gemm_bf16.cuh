@@ -524,11 +524,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (last) {
             __threadfence();
             // [splits][BN rows][128 columns] fp32 -> out.  Thread = 4 consecutive columns
-            // of every fourth row; 16-byte loads, 8 rows x all slices in flight per pass.
+            // of every fourth row; 16-byte loads, up to 16 rows of one slice in flight per thread.
             const float* base = args.ws + size_t(t.tile_id) * args.splits * (size_t(BN) * kBlockP);
             const int c4 = (epi_tid & 31) * 4;
             const int rgrp = epi_tid >> 5;  // 0..3
-            constexpr int kRowsPerPass = 8;
+            constexpr int kRowsPerPass = BN >= 128 ? 16 : (BN >= 32 ? 8 : 4);
             const bool vec_store = (args.ldo % 4 == 0) &&
                                    ((reinterpret_cast<uintptr_t>(args.out) & 7) == 0);
             for (int r0 = rgrp; r0 < t.rows_valid; r0 += 4 * kRowsPerPass) {
