@@ -509,7 +509,7 @@ def run_b200_arm(args) -> None:
                 "timing": "CUDA events around each launch, K eager steps right after the graph-replayed timed region",
                 "traffic": TRAFFIC_OVER_ALGORITHMIC * sum(
                     2.0 * (m * k + n * k / world + m * n / world) for (m, n, k) in dense_shapes) / len(dense_shapes),
-                "traffic_note": "DRAM bytes per launch: ncu capture of gemm:4096x8192x4096 (217.7 MB measured vs "
+                "traffic_note": "DRAM bytes per launch: ncu capture of gemm:4096x8192x4096 (216.2 MB measured vs "
                                 "167.8 MB algorithmic) scaled by algorithmic bytes to the average dense launch",
             },
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
