@@ -52,7 +52,7 @@ int launch_gemm(const CUtensorMap& mp, const CUtensorMap& mq, const GemmArgs& ar
   return launch_overlapped(kern, dim3(grid), dim3(kGemmThreads), smem, st, mp, mq, args);
 }
 
-constexpr int kSplitCounterSlots = 4096;  // split-K arrival counters at the head of a workspace
+constexpr int kSplitCounterSlots = 2 * kSplitTileSlots;  // split-K counters at the head of a workspace
 
 // Split of the last, partial wave of a CTA-pair launch: the `units % pairs` tiles left over
 // after the full rounds are cut into `slices` K slices each, one slice per pair.
@@ -217,14 +217,19 @@ SwapPlan plan_swap(int M, int N, int K, int sms) {
   p.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   p.tiles = ceil_div_h(N, kBlockP) * ceil_div_h(M, p.bn);
   const int k_blocks = ceil_div_h(K, kBlockK);
-  // one unit per CTA: as many K slices as fit the SMs, at least 4 K blocks per slice
+  // one unit per CTA: as many K slices as fit the SMs, at least 4 K blocks per slice.  Every
+  // slice adds 1 / splits of the tile, so the reduction does not grow with the slice count; the
+  // cap bounds the partial-sum traffic (splits x the tile in fp32, written and read once).
   int splits = sms / p.tiles;
   const int max_splits = k_blocks / 4 > 0 ? k_blocks / 4 : 1;
   if (splits > max_splits) splits = max_splits;
-  // the last slice to arrive adds splits x BN partial rows on its own: bound that tail
-  const int max_by_tail = 512 / p.bn;  // 4 slices of 128 rows ... 16 slices of <= 32 rows
-  if (splits > max_by_tail) splits = max_by_tail;
-  if (splits < 1 || p.tiles > kSplitCounterSlots) splits = 1;
+  static const int cap = [] {
+    const char* v = std::getenv("LUMEN_B200_SPLIT_CAP");  // measurement aid
+    const int c = v ? std::atoi(v) : 0;
+    return c > 0 ? c : 16;
+  }();
+  if (splits > cap) splits = cap;
+  if (splits < 1 || p.tiles > kSplitTileSlots) splits = 1;
   p.splits = splits;
   // the counters own a fixed region at the head of the scratch buffer, so that partial
   // sums of one shape never land where another shape keeps its counters
@@ -243,6 +248,11 @@ using namespace b200;
 // leave most CTA pairs idle (e.g. one GPU's column shard of a modest GEMM).
 static bool takes_streaming_path(int M, int N, int K, int sms) {
   if (M <= 128) return true;
+  static const int forced = [] {
+    const char* v = std::getenv("LUMEN_B200_GEMM_SMALL");  // measurement aid: "pair" / "stream"
+    return (v && v[0] == 'p') ? 1 : (v && v[0] == 's') ? 2 : 0;
+  }();
+  if (forced == 1) return false;
   const long long pair_units =
       static_cast<long long>((M + kPairTileM - 1) / kPairTileM) * ((N + 255) / 256);
   const long long swap_tiles = static_cast<long long>((N + kBlockP - 1) / kBlockP) * ((M + 127) / 128);

@@ -35,8 +35,11 @@ enum GemmWaitCode {
   kWaitFullStage = 2,
   kWaitTmemEmpty = 3,
   kWaitTmemFull = 4,
-  kWaitSlices = 5,  // CTA pairs: the other K slices of a split tile did not arrive
+  kWaitSlices = 5,  // the other K slices of a split tile did not arrive
 };
+
+// split-K counters: arrivals of tile i at counters[i], departures at counters[kSplitTileSlots + i]
+constexpr int kSplitTileSlots = 2048;
 
 struct GemmArgs {
   __nv_bfloat16* out;  // [rows_out, N] row-major, leading dimension ldo
@@ -511,38 +514,61 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (split_k) {
-          // the last slice to arrive adds all slices in slice order (deterministic)
+          // The slices of a tile add their partial tiles like a reduce-scatter: each waits until
+          // all have stored theirs, then sums 1 / splits of the tile's elements over the slices
+          // in slice order (so the result is the same from run to run) and stores them.  A launch
+          // has one unit per CTA and no more units than SMs, so every slice is running; the wait is
+          // bounded like the others.
           __threadfence();
           asm volatile("bar.sync 1, 128;" ::: "memory");
+          int* arrivals = args.counters + t.tile_id;
+          int* departures = args.counters + kSplitTileSlots + t.tile_id;
           if (epi_tid == 0) {
-            const int old = atomicAdd(&args.counters[t.tile_id], 1);
-            tail->last_flag = (old == args.splits - 1) ? 1 : 0;
-            if (old == args.splits - 1) args.counters[t.tile_id] = 0;  // ready for the next launch
+            atomicAdd(arrivals, 1);
+            int seen = 1;
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while (ld_acquire_gpu(arrivals) < args.splits) {
+              if ((++spins & 0xffu) == 0u) {
+                if (*ctx.cta_abort) {
+                  seen = 0;
+                  break;
+                }
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                  *ctx.cta_abort = 1;
+                  atomicCAS(ctx.status, 0, (kWaitSlices << 16) | static_cast<int>(blockIdx.x & 0xffffu));
+                  seen = 0;
+                  break;
+                }
+              }
+            }
+            tail->last_flag = seen;
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");
-          const bool last = tail->last_flag != 0;
-          if (last) {
+          const bool seen = tail->last_flag != 0;
+          if (seen) {
             __threadfence();
-            // [splits][BN rows][128 columns] fp32 -> out.  Thread = 4 consecutive columns
-            // of every fourth row; 16-byte loads, up to 16 rows of one slice in flight per thread.
+            // the valid rows of the tile as float4 elements, [row][32]; this slice's share of them
             const float* base = args.ws + size_t(t.tile_id) * args.splits * (size_t(BN) * kBlockP);
-            const int c4 = (epi_tid & 31) * 4;
-            const int rgrp = epi_tid >> 5;  // 0..3
-            constexpr int kRowsPerPass = BN >= 128 ? 16 : (BN >= 32 ? 8 : 4);
+            const int total4 = t.rows_valid * (kBlockP / 4);
+            const int share = (total4 + args.splits - 1) / args.splits;
+            const int first = t.split * share;
+            const int end = min(first + share, total4);
+            constexpr int kInFlight = 4;
             const bool vec_store = (args.ldo % 4 == 0) &&
                                    ((reinterpret_cast<uintptr_t>(args.out) & 7) == 0);
-            for (int r0 = rgrp; r0 < t.rows_valid; r0 += 4 * kRowsPerPass) {
-              float4 acc[kRowsPerPass];
+            for (int i0 = first + epi_tid; i0 < end; i0 += 128 * kInFlight) {
+              float4 acc[kInFlight];
 #pragma unroll
-              for (int i = 0; i < kRowsPerPass; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int i = 0; i < kInFlight; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
               for (int s = 0; s < args.splits; ++s) {
-                const float* slice = base + size_t(s) * (size_t(BN) * kBlockP) + c4;
-                float4 v[kRowsPerPass];
+                const float4* slice = reinterpret_cast<const float4*>(base + size_t(s) * (size_t(BN) * kBlockP));
+                float4 v[kInFlight];
 #pragma unroll
-                for (int i = 0; i < kRowsPerPass; ++i)  // all loads first: 8 in flight per thread
-                  v[i] = __ldcg(reinterpret_cast<const float4*>(slice + min(r0 + 4 * i, BN - 1) * kBlockP));
+                for (int i = 0; i < kInFlight; ++i) v[i] = __ldcg(slice + min(i0 + 128 * i, end - 1));
 #pragma unroll
-                for (int i = 0; i < kRowsPerPass; ++i) {
+                for (int i = 0; i < kInFlight; ++i) {
                   acc[i].x += v[i].x;
                   acc[i].y += v[i].y;
                   acc[i].z += v[i].z;
@@ -550,9 +576,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
               }
 #pragma unroll
-              for (int i = 0; i < kRowsPerPass; ++i) {
-                const int r = r0 + 4 * i;
-                if (r >= t.rows_valid) continue;
+              for (int i = 0; i < kInFlight; ++i) {
+                const int idx = i0 + 128 * i;
+                if (idx >= end) continue;
+                const int r = idx / (kBlockP / 4);
+                const int c4 = (idx % (kBlockP / 4)) * 4;
                 __nv_bfloat16* o = args.out + size_t(t.out_row + r) * args.ldo + t.out_col + c4;
                 if (vec_store && c4 + 4 <= t.cols_valid) {
                   uint2 q;
@@ -568,7 +596,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
             }
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");  // last_flag is reused by the next unit
+          asm volatile("bar.sync 1, 128;" ::: "memory");  // all reads done; last_flag is reused by the next unit
+          if (epi_tid == 0 && seen) {
+            // the last slice to have read resets both counters for the next launch
+            if (atomicAdd(departures, 1) == args.splits - 1) {
+              *departures = 0;
+              *arrivals = 0;
+            }
+          }
+          if (!seen) ok = false;
         }
       }
       // hand the accumulator buffer back to the MMA issuer
