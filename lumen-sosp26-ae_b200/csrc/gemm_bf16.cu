@@ -84,11 +84,11 @@ PairTailPlan plan_pair_tail(int units, int pairs, int K, int bn) {
 
 // dense GEMM on CTA pairs (clusters of 2); grid = 2 CTAs per co-resident cluster.  With a
 // workspace that is large enough, the last partial wave is split along K.
-template <int STAGES, int BN>
+template <int STAGES, int BN, bool GROUPED = false, bool GATED = false>
 int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args_in, int units,
                      void* workspace, size_t workspace_bytes, cudaStream_t st) {
-  auto kern = gemm_bf16_pair_kernel<STAGES, BN>;
-  constexpr size_t smem = gemm_pair_smem_bytes<STAGES, BN>();
+  auto kern = gemm_bf16_pair_kernel<STAGES, BN, GROUPED, GATED>;
+  constexpr size_t smem = gemm_pair_smem_bytes<STAGES, BN, GROUPED>();
   static_assert(smem <= 227 * 1024, "stage ring does not fit shared memory");
   static bool configured[64] = {};
   static int max_clusters[64] = {};
@@ -113,6 +113,8 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
   GemmArgs args = args_in;
   args.splits = 1;
   args.tail_first = units;
+  if (GROUPED)  // the unit count is on the device: one resident pair per two SMs
+    return launch_overlapped(kern, dim3(2 * max_clusters[dev]), dim3(kGemmThreads), smem, st, ma, mb, args);
   int work = units;
   const PairTailPlan plan = plan_pair_tail(units, max_clusters[dev], args.K, BN);
   constexpr size_t counter_bytes = size_t(kSplitCounterSlots) * sizeof(int);
@@ -169,6 +171,18 @@ bool use_pair_grouped() {
     cached = (v && v[0] == 'p') ? 1 : 0;
   }
   return cached == 1;
+}
+
+// Rows per expert (the caller's hint) from which the expert GEMMs run on CTA pairs with the tokens
+// on the 256 accumulator rows; LUMEN_B200_MOE_PAIR_ROWS overrides (0 = never).
+int token_pair_min_rows() {
+  static const int rows = [] {
+    const char* v = std::getenv("LUMEN_B200_MOE_PAIR_ROWS");
+    if (!v) return 768;
+    const int r = std::atoi(v);
+    return r > 0 ? r : (1 << 30);
+  }();
+  return rows;
 }
 
 // Width of the pair tile.  128-column tiles would cut the idle tail of the last wave in
@@ -423,6 +437,14 @@ static int grouped_gemm_impl(const void* acts, const void* weights, void* out, c
     if (encode_tmap_bf16_2d(&mq_tail, acts, max_rows, K, K, kPgTailBox) != 0) return LUMEN_B200_ECUDA;
     return gated ? launch_gemm_pair_grouped<5, true>(mp, mq, mq_tail, args, st)
                  : launch_gemm_pair_grouped<6, false>(mp, mq, mq_tail, args, st);
+  }
+  if (rows_hint >= token_pair_min_rows() && !out_row_ptrs) {
+    // many rows per expert: CTA pairs, 256 token rows x 256 weight rows per unit (gated: 64 gate +
+    // 64 up rows per CTA), the tile shape that feeds the tensor core at full rate
+    if (encode_tmap_bf16_2d(&mp, acts, max_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
+    if (encode_tmap_bf16_2d(&mq, weights, w_total_rows, K, K, gated ? 64 : 128) != 0) return LUMEN_B200_ECUDA;
+    return gated ? launch_gemm_pair<6, 256, true, true>(mp, mq, args, 0, nullptr, 0, st)
+                 : launch_gemm_pair<6, 256, true, false>(mp, mq, args, 0, nullptr, 0, st);
   }
   if (rows_hint > 128) {
     // tokens on the TMEM lanes, 128 rows per unit

@@ -32,7 +32,7 @@ __host__ __device__ constexpr int pair_stage_bytes() {
   return kBlockP * kBlockK * 2 + (BN / 2) * kBlockK * 2;
 }
 
-template <int STAGES>
+template <int STAGES, bool GROUPED = false>
 struct PairSmemTail {
   uint64_t full[STAGES];      // leader's copy is the one in use (expects both CTAs' bytes)
   uint64_t empty[STAGES];     // each CTA waits on its own copy
@@ -40,11 +40,12 @@ struct PairSmemTail {
   uint64_t tmem_empty[2];     // leader's copy: 8 arrivals = 4 epilogue warps x 2 CTAs
   uint32_t tmem_slot;
   int abort_flag;
+  int unit_start[GROUPED ? kMaxExperts + 1 : 1];  // grouped: first unit of each expert
 };
 
-template <int STAGES, int BN>
+template <int STAGES, int BN, bool GROUPED = false>
 constexpr size_t gemm_pair_smem_bytes() {
-  return 1024 + size_t(STAGES) * pair_stage_bytes<BN>() + sizeof(PairSmemTail<STAGES>);
+  return 1024 + size_t(STAGES) * pair_stage_bytes<BN>() + sizeof(PairSmemTail<STAGES, GROUPED>);
 }
 
 // status code: the two CTAs of a pair were given different TMEM base columns
@@ -69,10 +70,46 @@ __device__ __forceinline__ PairUnit pair_decode(int u, int tiles_m, int tiles_n)
 
 // One piece of work of a pair: an output tile over K blocks [kb0, kb1).
 struct PairWork {
-  int m0, n0;
+  int m0, n0;         // first A row of the tile; first output column
+  int b_row;          // first B (weight) row of the tile (grouped: inside the expert's block)
+  int rows_valid;     // output rows of the tile that exist, counted from m0
   int kb0, kb1;
   int slice, slices;  // slices == 1: the whole K range, stored directly
   int tail_idx;       // index of the tile among the split ones
+};
+
+// Grouped (expert by expert) work of the pair kernel, tokens on the 256 accumulator rows: the
+// units of expert e are [unit_start[e], unit_start[e + 1]), 256-row token tile fastest so that
+// pairs running together share a weight tile in L2.  A gated tile holds 64 gate + 64 up weight
+// rows per CTA and produces BN / 2 output columns.
+template <int BN, bool GATED>
+struct PairGroupedDecoder {
+  static constexpr int kOutCols = GATED ? BN / 2 : BN;
+  const GemmArgs& a;
+  const int* unit_start;
+  int cursor = 0;
+  __device__ PairGroupedDecoder(const GemmArgs& args, const int* us) : a(args), unit_start(us) {}
+  __device__ PairWork decode(int u, int k_blocks) {
+    int e = cursor;
+    while (u >= unit_start[e + 1]) ++e;
+    cursor = e;
+    const int local = u - unit_start[e];
+    const int cnt = a.expert_counts[e];
+    const int act_tiles = ceil_div(cnt, kPairTileM);
+    const int w_tile = local / act_tiles;
+    const int at = local - w_tile * act_tiles;
+    PairWork r;
+    r.m0 = a.expert_offsets[e] + at * kPairTileM;
+    r.rows_valid = cnt - at * kPairTileM;
+    r.n0 = w_tile * kOutCols;
+    r.b_row = e * a.w_rows_per_expert + r.n0;
+    r.kb0 = 0;
+    r.kb1 = k_blocks;
+    r.slice = 0;
+    r.slices = 1;
+    r.tail_idx = 0;
+    return r;
+  }
 };
 
 template <int BN>
@@ -97,16 +134,22 @@ __device__ __forceinline__ PairWork pair_work(int w, int tiles_m, int tiles_n, i
   const PairUnit t = pair_decode<BN>(u, tiles_m, tiles_n);
   r.m0 = t.m0;
   r.n0 = t.n0;
+  r.b_row = t.n0;
+  r.rows_valid = 1 << 30;  // dense: rows are bounded by args.M
   return r;
 }
 
 // BN = 256 or 128 output columns per tile (the narrower tile halves the unit of work, which
 // matters when the tile count is a small non-multiple of the 74 CTA pairs).
-template <int STAGES, int BN>
+// GROUPED: A = the routed rows of all experts, B = the stacked expert weights, units from the
+// expert counts on the device (GATED: SiLU(gate) * up in the epilogue); the map of B then has
+// boxes of BN / 4 rows.
+template <int STAGES, int BN, bool GROUPED = false, bool GATED = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                           const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
-  using Tail = PairSmemTail<STAGES>;
+  static_assert(!GATED || GROUPED, "the gated epilogue belongs to the expert GEMM");
+  using Tail = PairSmemTail<STAGES, GROUPED>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem_aligned = smem_raw + (smem_base - smem_u32(smem_raw));
@@ -138,6 +181,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   // nothing above reads or writes global memory: it may overlap the previous kernel's tail
   griddep_wait();
   griddep_launch_dependents();
+  if constexpr (GROUPED) {
+    // unit_start[e] = units of the experts before e; warp 0 scans the counts
+    if (warp == 0) {
+      const int w_tiles = ceil_div(args.N, PairGroupedDecoder<BN, GATED>::kOutCols);
+      int carry = 0;
+      for (int base = 0; base < args.num_experts; base += 32) {
+        const int e = base + lane;
+        const int v = (e < args.num_experts) ? ceil_div(args.expert_counts[e], kPairTileM) * w_tiles : 0;
+        int incl = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int o = __shfl_up_sync(0xffffffffu, incl, d);
+          if (lane >= d) incl += o;
+        }
+        if (e < args.num_experts) tail->unit_start[e] = carry + incl - v;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) tail->unit_start[args.num_experts] = carry;
+    }
+  }
   tc_fence_before_sync();
   __syncthreads();
   cluster_sync_all();  // barriers of both CTAs are initialised before any remote arrival
@@ -155,16 +218,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       atomicCAS(args.status, 0, (kPairTmemMismatch << 16) | static_cast<int>(blockIdx.x & 0xffffu));
     }
   }
-  const int tiles_m = ceil_div(args.M, kPairTileM);
-  const int tiles_n = ceil_div(args.N, BN);
-  const int total_units = tiles_m * tiles_n;
+  const int tiles_m = GROUPED ? 0 : ceil_div(args.M, kPairTileM);
+  const int tiles_n = GROUPED ? 0 : ceil_div(args.N, BN);
+  const int total_units = GROUPED ? tail->unit_start[args.num_experts] : tiles_m * tiles_n;
   const int k_blocks = ceil_div(args.K, kBlockK);
   const int pair_id = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   // pieces of work: whole tiles [0, tail_first), then `slices` K slices of each later tile
-  const int slices = args.splits > 1 ? args.splits : 1;
+  const int slices = (!GROUPED && args.splits > 1) ? args.splits : 1;
   const int tail_first = slices > 1 ? args.tail_first : total_units;
   const int total_work = tail_first + (total_units - tail_first) * slices;
+  // each role walks the work list with its own decoder (the grouped one keeps a cursor)
+  auto make_decoder = [&]() { return PairGroupedDecoder<BN, GATED>(args, tail->unit_start); };
+  auto decode = [&](PairGroupedDecoder<BN, GATED>& dec, int w) {
+    if constexpr (GROUPED) {
+      return dec.decode(w, k_blocks);
+    } else {
+      return pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
+    }
+  };
 
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) ======================
@@ -172,10 +244,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      auto dec = make_decoder();
       for (int w = pair_id; w < total_work && ok; w += num_pairs) {
-        const PairWork t = pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
+        const PairWork t = decode(dec, w);
         const int a_row = t.m0 + int(rank) * kBlockP;
-        const int b_row = t.n0 + int(rank) * (BN / 2);
+        // B rows of this CTA: BN / 2 consecutive ones, or for a gated tile BN / 4 gate rows and the
+        // BN / 4 up rows that belong to them
+        const int b_row = t.b_row + int(rank) * (GATED ? BN / 4 : BN / 2);
         for (int kb = t.kb0; kb < t.kb1; ++kb) {
           if (!mbar_wait(smem_u32(&tail->empty[stage]), phase ^ 1u, ctx, kWaitEmptyStage)) {
             ok = false;
@@ -187,6 +262,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const uint32_t sb = sa + kBlockP * kBlockK * 2;
           tma_load_2d_pair(sa, &map_a, leader_full, kb * kBlockK, a_row);
           tma_load_2d_pair(sb, &map_b, leader_full, kb * kBlockK, b_row);
+          if constexpr (GATED)
+            tma_load_2d_pair(sb + (BN / 4) * kBlockK * 2, &map_b, leader_full, kb * kBlockK,
+                             b_row + args.up_row_offset);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -202,8 +280,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
+      auto dec = make_decoder();
       for (int w = pair_id; w < total_work && ok; w += num_pairs, ++it) {
-        const PairWork t = pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
+        const PairWork t = decode(dec, w);
         const int buf = it & 1;
         const uint32_t buf_phase = (it >> 1) & 1;
         if (!mbar_wait(smem_u32(&tail->tmem_empty[buf]), buf_phase ^ 1u, ctx, kWaitTmemEmpty)) {
@@ -242,8 +321,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const bool vec_ok = (args.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
     int it = 0;
     bool ok = true;
+    auto dec = make_decoder();
     for (int w = pair_id; w < total_work && ok; w += num_pairs, ++it) {
-      const PairWork t = pair_work<BN>(w, tiles_m, tiles_n, k_blocks, tail_first, slices);
+      const PairWork t = decode(dec, w);
       const int buf = it & 1;
       const uint32_t buf_phase = (it >> 1) & 1;
       if (!mbar_wait(smem_u32(&tail->tmem_full[buf]), buf_phase, ctx, kWaitTmemFull)) {
@@ -254,8 +334,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       tc_fence_after_sync();
       const uint32_t t_acc = tmem_base + (uint32_t(quad * 32) << 16) + buf * BN;
       const int row = t.m0 + int(rank) * kBlockP + p;
-      const bool row_ok = row < args.M;
-      const int cols_valid = min(BN, args.N - t.n0);
+      const bool row_ok = GROUPED ? (int(rank) * kBlockP + p < t.rows_valid) : (row < args.M);
+      const int cols_valid = min(GATED ? BN / 2 : BN, args.N - t.n0);
       __nv_bfloat16* orow = args.out + size_t(row) * args.ldo + t.n0;
       // 32 fp32 values of this thread's row, columns [c * 32, c * 32 + 32) of the tile -> bf16 -> C
       auto store_chunk = [&](const uint32_t (&v)[32], int c) {
@@ -278,12 +358,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         }
       };
       if (t.slices == 1) {
+        if constexpr (GATED) {
+          // accumulator columns of this CTA's rows: [gate of CTA 0 | up of CTA 0 | gate of CTA 1 |
+          // up of CTA 1], BN / 4 each; output chunk c = columns [c * 32, c * 32 + 32) of the tile
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_acc + c * 32, v);
-          tmem_ld_wait();
-          store_chunk(v, c);
+          for (int c = 0; c < BN / 64; ++c) {
+            const int half = (c * 32) / (BN / 4);
+            const int within = c * 32 - half * (BN / 4);
+            uint32_t g[32], u[32];
+            tmem_ld_32x32b_x32(t_acc + half * (BN / 2) + within, g);
+            tmem_ld_32x32b_x32(t_acc + half * (BN / 2) + BN / 4 + within, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              g[j] = __float_as_uint(silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j])));
+            store_chunk(g, c);
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(t_acc + c * 32, v);
+            tmem_ld_wait();
+            store_chunk(v, c);
+          }
         }
         tc_fence_before_sync();
         __syncwarp();

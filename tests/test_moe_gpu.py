@@ -148,6 +148,8 @@ def test_forward_golden(cuda_pkg, case, k, router):
     (400, 512, 256, 8, 2, True),        # 100 rows per expert: weight-major, MMA N sized per unit
     (1024, 512, 256, 8, 2, True),       # 256 rows per expert: token-major orientation
     (700, 384, 640, 4, 2, True),        # ragged tiles in every dimension
+    (3300, 256, 384, 4, 1, True),       # ~825 rows per expert: CTA pairs, 256-row token tiles, ragged
+    (1500, 320, 192, 2, 2, False),      # 1500 rows per expert, columns that do not fill a tile
 ])
 def test_forward_matches_oracle(cuda_pkg, T, H, I, E, k, router):
     d, op, out, ids, w = moe_case(cuda_pkg, T, H, I, E, k, 20260319 + T, router)
