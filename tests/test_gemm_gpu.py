@@ -77,6 +77,21 @@ def test_split_last_wave_matches_oracle_rows(cuda_pkg, m, n, k):
     torch.testing.assert_close(out[rows.to(dev)].cpu().float(), want.float(), rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("m,n,k", [(128, 512, 4096), (16, 1792, 14336), (100, 1000, 4104)])
+def test_split_k_slices_add_in_a_fixed_order(cuda_pkg, m, n, k):
+    """Few rows, long K: up to 16 K slices per tile add their partial sums like a reduce-scatter.
+    The order of the additions is fixed, so two runs agree bit for bit; rows against the oracle."""
+    dev = torch.device("cuda:0")
+    a, b = gemm_oracle.gemm_inputs(m, n, k, seed=7 + m + n + k)
+    ad, bd = a.to(dev), b.to(dev)
+    out = cuda_pkg.gemm_pipeline_transposed_b(ad, bd)
+    again = cuda_pkg.gemm_pipeline_transposed_b(ad, bd)
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+    assert torch.equal(out, again)
+    torch.testing.assert_close(out.cpu().float(), gemm_oracle.gemm_reference(a, b).float(), rtol=RTOL, atol=ATOL)
+
+
 def test_split_last_wave_is_exact_on_integers_and_optional(cuda_pkg):
     """Integer-valued operands: every partial sum is exact, so the split result equals the
     oracle bit for bit; the same call without a workspace (no split) must agree."""
