@@ -18,8 +18,9 @@ _workspaces: dict[int, torch.Tensor] = {}
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
     """Split-K scratch of `device`, zero-filled when created and grown on demand (never
-    shrunk).  One buffer per device: GEMMs that take the split-K path must not overlap on
-    the GPU (launch them on one stream, or pass explicit workspaces through the C-ABI).
+    shrunk).  One buffer per device: GEMMs that use it (few activation rows, or a large
+    problem whose last wave of tiles is split over K) must not overlap on the GPU (launch
+    them on one stream, or pass explicit workspaces through the C-ABI).
     It is created by the first call that needs it, so make that call before capturing a
     CUDA graph; replays then reuse it without a fill."""
     if nbytes == 0:
