@@ -117,6 +117,25 @@ def test_split_last_wave_is_exact_on_integers_and_optional(cuda_pkg):
     assert torch.equal(out, plain)
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_column_shards_of_the_sweep(cuda_pkg, world):
+    """Every shape of the benchmark sweep at the width one rank of `world` GPUs computes (N / world
+    columns): narrow problems take other tile plans (K slices, split last waves) than the full-width
+    ones.  Checked on the device against an fp32 matmul of the same bf16 operands."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(20260312)
+    for m in (1, 16, 128, 1024, 8192):
+        for (n, k) in ((4096, 4096), (14336, 4096), (4096, 14336), (6144, 4096)):
+            ns = n // world
+            a = torch.randn((m, k), device=dev, dtype=torch.bfloat16, generator=g)
+            b = (torch.randn((ns, k), device=dev, dtype=torch.float32, generator=g) * 0.02).to(torch.bfloat16)
+            out = cuda_pkg.gemm_pipeline_transposed_b(a, b)
+            want = a.float() @ b.float().T
+            torch.testing.assert_close(out.float(), want, rtol=RTOL, atol=ATOL, msg=lambda s_: f"{m}x{ns}x{k}: {s_}")
+    torch.cuda.synchronize()
+    assert cuda_pkg.device_status() == 0
+
+
 def test_caller_owned_output_and_pitch(cuda_pkg):
     dev = torch.device("cuda:0")
     a, b = gemm_oracle.gemm_inputs(200, 264, 128, seed=3)
