@@ -260,16 +260,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           as[i] = __ldg(args.act_scale_t + size_t(kb) * args.max_rows + row);
         }
       };
-      float as_next[BN / 32];
-      load_act_scales(0, as_next);
+      // The scales of a K block are requested three blocks ahead and handed down by register
+      // copies, so that a stage never waits for them (a load issued in the stage that uses it
+      // costs a trip to L2 or HBM per stage, more than the stage's own work).
+      struct Scales {
+        float as[BN / 32];
+        float wg, wu;
+      };
+      auto load_scales = [&](int kb, Scales& sc) {
+        if (kb >= kb_total) return;
+        load_act_scales(kb, sc.as);
+        sc.wg = __ldg(ws_g + kb);
+        sc.wu = GATED ? __ldg(ws_u + kb) : 0.f;
+      };
+      Scales s0{}, s1{}, s2{};
+      load_scales(0, s0);
+      load_scales(1, s1);
+      load_scales(2, s2);
       for (int kb = 0; kb < kb_total; ++kb, ++it) {
         const uint32_t b = it & 1u;
         float as[BN / 32];
 #pragma unroll
-        for (int i = 0; i < BN / 32; ++i) as[i] = as_next[i];
-        const float wg = __ldg(ws_g + kb) * args.scale_mul;
-        const float wu = GATED ? __ldg(ws_u + kb) * args.scale_mul : 0.f;
-        if (kb + 1 < kb_total) load_act_scales(kb + 1, as_next);
+        for (int i = 0; i < BN / 32; ++i) as[i] = s0.as[i];
+        const float wg = s0.wg * args.scale_mul;
+        const float wu = s0.wu * args.scale_mul;
+        s0 = s1;
+        s1 = s2;
+        load_scales(kb + 3, s2);
         if (!mbar_wait(smem_u32(&tail->part_full[b]), (it >> 1) & 1u, ctx, kF8WaitPartFull)) {
           ok = false;
           break;
