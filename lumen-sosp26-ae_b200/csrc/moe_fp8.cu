@@ -71,6 +71,10 @@ struct F8Tail {
   int unit_start[kMaxExperts + 1];
   float warp_max[4][BN];  // quantising epilogue: per-warp maxima of |h| per token
   float col_max[BN];
+  // per promotion warp: this K block's combined scales (token scale x weight-block scale) of the
+  // BN tokens, for the gate rows and for the up rows, read back as broadcasts
+  alignas(16) float scale_g[4][BN];
+  alignas(16) float scale_u[4][BN];
 };
 
 template <int BN, int STAGES, bool GATED>
@@ -287,6 +291,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         s0 = s1;
         s1 = s2;
         load_scales(kb + 3, s2);
+        // lane l knows the scale of token 32 c + l; every lane needs all of them: through shared
+        // memory, as 16-byte broadcast reads (a shuffle and two multiplies per token cost more
+        // than the two multiply-adds they feed)
+        float* sg = tail->scale_g[quad];
+        float* su = tail->scale_u[quad];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          sg[c * 32 + lane] = as[c] * wg;
+          if constexpr (GATED) su[c * 32 + lane] = as[c] * wu;
+        }
+        __syncwarp();
         if (!mbar_wait(smem_u32(&tail->part_full[b]), (it >> 1) & 1u, ctx, kF8WaitPartFull)) {
           ok = false;
           break;
@@ -304,21 +319,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tmem_ld_32x32b_x32(t_part + BN + c * 32, w);
               tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float s = __shfl_sync(0xffffffffu, as[c], j);
-                acc[c * 32 + j] = fmaf(__uint_as_float(v[j]), s * wg, acc[c * 32 + j]);
-                acc[BN + c * 32 + j] = fmaf(__uint_as_float(w[j]), s * wu, acc[BN + c * 32 + j]);
+              for (int j = 0; j < 32; j += 4) {
+                const float4 g4 = *reinterpret_cast<const float4*>(sg + c * 32 + j);
+                const float4 u4 = *reinterpret_cast<const float4*>(su + c * 32 + j);
+                acc[c * 32 + j + 0] = fmaf(__uint_as_float(v[j + 0]), g4.x, acc[c * 32 + j + 0]);
+                acc[c * 32 + j + 1] = fmaf(__uint_as_float(v[j + 1]), g4.y, acc[c * 32 + j + 1]);
+                acc[c * 32 + j + 2] = fmaf(__uint_as_float(v[j + 2]), g4.z, acc[c * 32 + j + 2]);
+                acc[c * 32 + j + 3] = fmaf(__uint_as_float(v[j + 3]), g4.w, acc[c * 32 + j + 3]);
+                acc[BN + c * 32 + j + 0] = fmaf(__uint_as_float(w[j + 0]), u4.x, acc[BN + c * 32 + j + 0]);
+                acc[BN + c * 32 + j + 1] = fmaf(__uint_as_float(w[j + 1]), u4.y, acc[BN + c * 32 + j + 1]);
+                acc[BN + c * 32 + j + 2] = fmaf(__uint_as_float(w[j + 2]), u4.z, acc[BN + c * 32 + j + 2]);
+                acc[BN + c * 32 + j + 3] = fmaf(__uint_as_float(w[j + 3]), u4.w, acc[BN + c * 32 + j + 3]);
               }
             } else {
               tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float s = __shfl_sync(0xffffffffu, as[c], j);
-                acc[c * 32 + j] = fmaf(__uint_as_float(v[j]), s * wg, acc[c * 32 + j]);
+              for (int j = 0; j < 32; j += 4) {
+                const float4 g4 = *reinterpret_cast<const float4*>(sg + c * 32 + j);
+                acc[c * 32 + j + 0] = fmaf(__uint_as_float(v[j + 0]), g4.x, acc[c * 32 + j + 0]);
+                acc[c * 32 + j + 1] = fmaf(__uint_as_float(v[j + 1]), g4.y, acc[c * 32 + j + 1]);
+                acc[c * 32 + j + 2] = fmaf(__uint_as_float(v[j + 2]), g4.z, acc[c * 32 + j + 2]);
+                acc[c * 32 + j + 3] = fmaf(__uint_as_float(v[j + 3]), g4.w, acc[c * 32 + j + 3]);
               }
             }
           }
         }
+        __syncwarp();  // every lane has read the scales before the next K block overwrites them
         // the partial is in registers: hand its buffer back to the MMA issuer
         tc_fence_before_sync();
         __syncwarp();
