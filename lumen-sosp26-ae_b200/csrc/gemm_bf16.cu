@@ -438,11 +438,11 @@ static int grouped_gemm_impl(const void* acts, const void* weights, void* out, c
     return gated ? launch_gemm_pair_grouped<5, true>(mp, mq, mq_tail, args, st)
                  : launch_gemm_pair_grouped<6, false>(mp, mq, mq_tail, args, st);
   }
-  // (and only with at least four rounds of 256 x 256 tiles over the CTA pairs: with one or two
+  // (and only with at least three rounds of 256 x 256 tiles over the CTA pairs: with one or two
   // experts per GPU the coarser tiles leave the last round mostly empty)
   const long long pair_units = static_cast<long long>(E) * ((rows_hint + kPairTileM - 1) / kPairTileM) *
                                ((N + (gated ? 127 : 255)) / (gated ? 128 : 256));
-  if (rows_hint >= token_pair_min_rows() && !out_row_ptrs && pair_units >= 4LL * (sms / 2)) {
+  if (rows_hint >= token_pair_min_rows() && !out_row_ptrs && pair_units >= 3LL * (sms / 2)) {
     // many rows per expert: CTA pairs, 256 token rows x 256 weight rows per unit (gated: 64 gate +
     // 64 up rows per CTA), the tile shape that feeds the tensor core at full rate
     if (encode_tmap_bf16_2d(&mp, acts, max_rows, K, K, kBlockP) != 0) return LUMEN_B200_ECUDA;
